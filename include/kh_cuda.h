@@ -1,0 +1,151 @@
+/*
+ * kh_cuda.h — C ABI of libkhcuda.so, the CUDA executor of kleinhirn Plans on B200 (sm_100a).
+ *
+ * The library is the device half of a `CudaBackend` that implements kleinhirn's `Backend` /
+ * `PlanRunner` interface (src/backend.ts:14-46) beside src/webgpu-backend.ts and
+ * src/wasm-backend.ts. It consumes the unchanged execution Plan (src/plan/ir.ts:41-60),
+ * serialised as JSON, and the weights of the src/weights.ts loader (TensorDesc,
+ * src/weights.ts:7-17). A host binding (N-API addon for Node, ctypes for Python) wraps these
+ * functions one to one; no torch or other framework type appears in any signature.
+ *
+ * Conventions
+ * - Every function that can fail returns int status: KH_OK (0) or a KH_ERR_* code. The message
+ *   of the last failure on the calling thread is kh_last_error(); a binding turns a non-zero
+ *   status into a thrown error with that message (as answer() does for the WASM worker,
+ *   src/wasm-backend.ts:48-51).
+ * - A CUDA error during a run latches in the context: every later call on that context fails
+ *   with KH_ERR_STATE and the first message (mirrors failIfBroken, src/device.ts:79-81).
+ * - Buffers passed in are host memory owned by the caller and are copied before the call
+ *   returns (the WASM host copies inputs the same way, src/plan/wasm.ts:409-440); output
+ *   buffers are host memory owned by the caller.
+ * - One call in flight per plan (EncoderModel.enqueue serialises calls, src/encoder.ts:265-269).
+ *   Distinct plans of one context share the context's stream.
+ */
+#ifndef KH_CUDA_H
+#define KH_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct kh_ctx kh_ctx;
+typedef struct kh_plan kh_plan;
+typedef struct kh_bulk kh_bulk;
+
+enum kh_status {
+  KH_OK = 0,
+  KH_ERR_ARG = 1,   /* bad argument: sizes, null pointers, unknown tensor */
+  KH_ERR_PLAN = 2,  /* the plan cannot run here (Backend.check) */
+  KH_ERR_CUDA = 3,  /* a CUDA call failed */
+  KH_ERR_STATE = 4  /* an earlier CUDA error latched in the context */
+};
+
+enum kh_dtype { KH_F32 = 0, KH_F16 = 1 };
+
+/* Message of the last failure on this thread ("" when none). */
+const char* kh_last_error(void);
+
+/* Opens a context on the first of `devices` (n_devices >= 1). Replaces the device half of
+ * loadBackend / loadGpu (src/backend.ts:75-89, src/webgpu-backend.ts:53-108). */
+int kh_init(const int* devices, int n_devices, kh_ctx** out);
+
+/* Copies one weight tensor to the device: TensorDesc name, dtype (KH_F32 or KH_F16), shape
+ * (src/weights.ts:7-17) and its bytes from a verified shard (fetchShardBytes,
+ * src/weights.ts:150-173). One createBuffer + writeBuffer per tensor in the WebGPU loader
+ * (src/webgpu-backend.ts:53-101). The word table (keepOnCpu) is not added: it stays on the
+ * host, as in src/wasm-backend.ts:184. */
+int kh_add_tensor(kh_ctx* ctx, const char* name, int dtype, const int64_t* shape, int ndim, const void* bytes,
+                  size_t len);
+
+/* Backend.weightBytes (src/backend.ts:32-33): device bytes of the loaded weights. */
+int64_t kh_weight_bytes(const kh_ctx* ctx);
+
+/* Backend.check (src/backend.ts:34-35): KH_OK when the plan can run, KH_ERR_PLAN with the
+ * reason otherwise. Allocates nothing (src/plan/check.ts:119-124 checks before allocating). */
+int kh_check(kh_ctx* ctx, const char* plan_json, size_t len);
+
+/* Backend.runner (src/backend.ts:36): device buffers, derived weights and the launch list of
+ * one Plan (JSON of src/plan/ir.ts:41-60, buffer init blobs as base64 under "init_b64"). */
+int kh_plan_create(kh_ctx* ctx, const char* plan_json, size_t len, kh_plan** out);
+
+/* PlanRunner.length / batch / bytes and the output shape (Plan.output rows x cols). */
+int kh_plan_info(const kh_plan* plan, int* length, int* batch, int* out_rows, int* out_cols, int64_t* bytes);
+
+/* PlanRunner.upload (src/backend.ts:20, RunInput src/plan/executor.ts:25-32): word rows
+ * [batch * length * embeddingSize] in the plan's storage type (f16 bits for f16 plans, f32
+ * otherwise), mask f32 [batch * length], typeIds u32 [batch * length] (low 16 bits the type,
+ * high 16 bits the position row) or null when the plan has no typeIds input. Shorter inputs
+ * are accepted, as writeBuffer writes a prefix. */
+int kh_upload(kh_plan* plan, const void* emb, size_t emb_bytes, const float* mask, size_t mask_len,
+              const uint32_t* type_ids, size_t type_len);
+
+/* PlanRunner.run (src/backend.ts:21-23): one forward over `rows` rows — the real rows of a
+ * B = 1 call (1 <= rows <= length), or length * batch for a batch plan. */
+int kh_run(kh_plan* plan, int rows);
+
+/* PlanRunner.readOutput (src/backend.ts:24, src/plan/executor.ts:398-408): blocks until the
+ * run is done and writes out_rows * out_cols f32 values (f16 storage converted). */
+int kh_read_output(kh_plan* plan, float* out, size_t n);
+
+/* PlanRunner.destroy (src/backend.ts:27). */
+void kh_plan_destroy(kh_plan* plan);
+
+/* Backend.dispose (src/backend.ts:45). */
+void kh_destroy(kh_ctx* ctx);
+
+/* Backend.info (src/backend.ts:44): JSON with device name, SM count, memory, weight bytes.
+ * Returns the bytes needed including the terminating zero; writes at most `cap` bytes. */
+size_t kh_info(const kh_ctx* ctx, char* buf, size_t cap);
+
+/* The launch list of a plan as JSON (one entry per kernel launch of kh_run, with the plan ops
+ * it covers), for profiles and tests. Same size convention as kh_info. */
+size_t kh_plan_launches(const kh_plan* plan, char* buf, size_t cap);
+
+/* Per-launch device times in ms of one forward over `rows` rows (CUDA events around every
+ * launch), the CUDA counterpart of the WASM op profile (src/plan/wasm.ts:451-471) and of the
+ * WebGPU dispatch profile (src/plan/executor.ts:303-361). Writes min(n, launches) values. */
+int kh_profile(kh_plan* plan, int rows, float* ms, size_t n);
+
+/* ---- ragged bulk runs: many sequences per call, only the rows a text has ----
+ * Replaces the batch path of EncoderModel.runIdsBatch (src/encoder.ts:461-474), which pads to
+ * batch plans of at most 16 sequences at a 64-row stride (src/cache.ts:9-19, :81-83): here the
+ * sequences of one call are packed back to back and no padding row is computed.
+ * A bulk handle holds device room for `max_tokens` packed input rows and `max_seqs` sequences
+ * of one plan; its forward runs in chunks of at most `chunk_tokens` rows through one set of
+ * activation buffers. Every sequence has all its rows valid (mask 1) and at most
+ * plan.length rows. */
+int kh_bulk_create(kh_plan* plan, int64_t max_tokens, int max_seqs, int64_t chunk_tokens, kh_bulk** out);
+
+/* The sequences of the next run: n lengths in [1, plan.length], sum <= max_tokens. */
+int kh_bulk_set_lengths(kh_bulk* bulk, const int32_t* seq_lens, int n);
+
+/* Packed inputs of the sequences set last: word rows [sum(len) * embeddingSize] in the plan's
+ * storage type and, when the plan has a typeIds input, typeIds [sum(len)] (type in the low, the
+ * position row in the high 16 bits); type_ids may be null otherwise. Host to device copy. */
+int kh_bulk_upload(kh_bulk* bulk, const void* emb, size_t emb_bytes, const uint32_t* type_ids, size_t type_len);
+
+/* Device-side forward of every sequence (no host copies; returns when the launches are queued). */
+int kh_bulk_run(kh_bulk* bulk);
+
+/* Waits for the run and writes the outputs: one row of out_cols f32 per sequence for pooled
+ * heads (n_seqs * out_cols values), one per packed row for token heads (sum(len) * out_cols). */
+int kh_bulk_read(kh_bulk* bulk, float* out, size_t n);
+
+/* set_lengths + upload + run + read in one call. */
+int kh_run_batch(kh_bulk* bulk, const int32_t* seq_lens, int n, const void* emb, size_t emb_bytes,
+                 const uint32_t* type_ids, size_t type_len, float* out, size_t out_len);
+
+/* Device time in ms of the last kh_bulk_run (CUDA events on the context stream), and the
+ * number of kernel launches it made. */
+int kh_bulk_last_timing(const kh_bulk* bulk, float* ms, int64_t* launches);
+
+void kh_bulk_destroy(kh_bulk* bulk);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KH_CUDA_H */

@@ -1,0 +1,596 @@
+// C ABI of libkhcuda.so (include/kh_cuda.h). Each entry point catches every exception of the
+// runtime and turns it into a status code and a thread-local message.
+
+#include <algorithm>
+#include <cstring>
+#include <memory>
+#include <sstream>
+#include <string>
+#include <vector>
+
+#include "../../include/kh_cuda.h"
+#include "runtime.h"
+
+using kh::Ctx;
+
+struct kh_ctx {
+  std::unique_ptr<Ctx> c;
+};
+
+struct kh_plan {
+  kh_ctx* owner = nullptr;
+  kh::CompiledPlan cp;
+  kh::Exec ex;
+  std::vector<int32_t> htable;
+};
+
+struct kh_bulk {
+  kh_plan* plan = nullptr;
+  kh::Exec ex;               // chunk workspace
+  void* d_emb = nullptr;     // resident packed inputs
+  uint32_t* d_type = nullptr;
+  float* d_mask = nullptr;   // ones
+  float* d_out = nullptr;    // f32 outputs of every sequence (or row)
+  int64_t max_tokens = 0, chunk_tokens = 0;
+  int max_seqs = 0;
+  int32_t* d_table = nullptr;
+  int64_t table_cap = 0;
+  struct Chunk {
+    int64_t tok0 = 0, T = 0;
+    int seq0 = 0, S = 0;
+    int64_t word0 = 0;  // offset of the chunk's sequence table in d_table
+    kh::SeqTable seq;   // offsets inside the chunk table
+  };
+  std::vector<Chunk> chunks;
+  int n_seqs = 0;
+  int64_t n_tokens = 0;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  int64_t last_launches = 0;
+  ~kh_bulk();
+};
+
+namespace {
+
+thread_local std::string g_err;
+
+enum class Latch { No, Yes };
+
+template <class F>
+int guard(Ctx* c, Latch latch, F&& f) {
+  try {
+    if (c && !c->broken.empty()) {
+      g_err = "device error latched earlier: " + c->broken;
+      return KH_ERR_STATE;
+    }
+    if (c) KH_CUDA(cudaSetDevice(c->device));
+    f();
+    return KH_OK;
+  } catch (const kh::CudaError& e) {
+    g_err = e.what();
+    if (c && latch == Latch::Yes) c->broken = g_err;
+    return KH_ERR_CUDA;
+  } catch (const kh::PlanError& e) {
+    g_err = e.what();
+    return KH_ERR_PLAN;
+  } catch (const kh::ArgError& e) {
+    g_err = e.what();
+    return KH_ERR_ARG;
+  } catch (const std::exception& e) {
+    g_err = e.what();
+    return KH_ERR_ARG;
+  }
+}
+
+size_t put_string(const std::string& s, char* buf, size_t cap) {
+  if (buf && cap) {
+    const size_t n = std::min(cap - 1, s.size());
+    std::memcpy(buf, s.data(), n);
+    buf[n] = 0;
+  }
+  return s.size() + 1;
+}
+
+// Rebases the word offsets of a host sequence table onto its device copy.
+kh::SeqTable rebase(const kh::SeqTable& o, const int32_t* base) {
+  kh::SeqTable s = o;
+  s.start = base + (intptr_t)o.start;
+  s.len = base + (intptr_t)o.len;
+  s.row_pos = base + (intptr_t)o.row_pos;
+  s.tiles = base + (intptr_t)o.tiles;
+  return s;
+}
+
+std::string json_escape(const std::string& s) {
+  std::string o;
+  for (char c : s) {
+    if (c == '"' || c == '\\') o += '\\';
+    o += c;
+  }
+  return o;
+}
+
+}  // namespace
+
+kh_bulk::~kh_bulk() {
+  if (plan) cudaSetDevice(plan->owner->c->device);
+  cudaFree(d_emb);
+  cudaFree(d_type);
+  cudaFree(d_mask);
+  cudaFree(d_out);
+  cudaFree(d_table);
+  if (ev0) cudaEventDestroy(ev0);
+  if (ev1) cudaEventDestroy(ev1);
+}
+
+extern "C" {
+
+const char* kh_last_error(void) { return g_err.c_str(); }
+
+int kh_init(const int* devices, int n_devices, kh_ctx** out) {
+  if (!out || !devices || n_devices < 1) {
+    g_err = "kh_init: devices and out are required";
+    return KH_ERR_ARG;
+  }
+  *out = nullptr;
+  auto h = std::make_unique<kh_ctx>();
+  h->c = std::make_unique<Ctx>();
+  Ctx* c = h->c.get();
+  c->device = devices[0];
+  const int st = guard(nullptr, Latch::No, [&] {
+    int count = 0;
+    KH_CUDA(cudaGetDeviceCount(&count));
+    if (c->device < 0 || c->device >= count) throw kh::ArgError("kh_init: device " + std::to_string(c->device) +
+                                                                " outside the " + std::to_string(count) + " devices");
+    KH_CUDA(cudaSetDevice(c->device));
+    cudaDeviceProp prop;
+    KH_CUDA(cudaGetDeviceProperties(&prop, c->device));
+    if (prop.major != 10) throw kh::PlanError(std::string("kh_init: ") + prop.name + " is not an sm_100 device");
+    c->sms = prop.multiProcessorCount;
+    KH_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+  });
+  if (st != KH_OK) return st;
+  *out = h.release();
+  return KH_OK;
+}
+
+int kh_add_tensor(kh_ctx* ctx, const char* name, int dtype, const int64_t* shape, int ndim, const void* bytes,
+                  size_t len) {
+  if (!ctx || !name || (ndim > 0 && !shape) || (len && !bytes)) {
+    g_err = "kh_add_tensor: null argument";
+    return KH_ERR_ARG;
+  }
+  Ctx* c = ctx->c.get();
+  return guard(c, Latch::No, [&] {
+    if (dtype != KH_F32 && dtype != KH_F16) throw kh::ArgError(std::string("tensor ") + name + ": dtype " +
+                                                               std::to_string(dtype) + " is neither f32 nor f16");
+    if (c->tensors.count(name)) throw kh::ArgError(std::string("weight ") + name + " loaded twice");
+    kh::DevTensor t;
+    t.name = name;
+    t.dtype = dtype;
+    t.shape.assign(shape, shape + ndim);
+    const int64_t n = t.numel();
+    if (n < 0 || size_t(n) * (dtype == KH_F16 ? 2 : 4) != len)
+      throw kh::ArgError(std::string("tensor ") + name + ": " + std::to_string(len) + " bytes for " +
+                         std::to_string(n) + " elements");
+    t.bytes = len;
+    KH_CUDA(cudaMalloc(&t.ptr, std::max<size_t>(len, 16)));
+    KH_CUDA(cudaMemcpy(t.ptr, bytes, len, cudaMemcpyHostToDevice));
+    c->weight_bytes += int64_t(len);
+    c->tensors.emplace(t.name, t);
+  });
+}
+
+int64_t kh_weight_bytes(const kh_ctx* ctx) { return ctx ? ctx->c->weight_bytes : 0; }
+
+int kh_check(kh_ctx* ctx, const char* plan_json, size_t len) {
+  if (!ctx || !plan_json) {
+    g_err = "kh_check: null argument";
+    return KH_ERR_ARG;
+  }
+  Ctx* c = ctx->c.get();
+  return guard(c, Latch::No, [&] {
+    kh::Json plan;
+    try {
+      plan = kh::parse_json(plan_json, len);
+    } catch (const std::exception& e) {
+      throw kh::PlanError(e.what());
+    }
+    kh::plan_check(c, plan);
+  });
+}
+
+int kh_plan_create(kh_ctx* ctx, const char* plan_json, size_t len, kh_plan** out) {
+  if (!ctx || !plan_json || !out) {
+    g_err = "kh_plan_create: null argument";
+    return KH_ERR_ARG;
+  }
+  *out = nullptr;
+  Ctx* c = ctx->c.get();
+  auto p = std::make_unique<kh_plan>();
+  p->owner = ctx;
+  const int st = guard(c, Latch::No, [&] {
+    kh::Json plan;
+    try {
+      plan = kh::parse_json(plan_json, len);
+    } catch (const std::exception& e) {
+      throw kh::PlanError(e.what());
+    }
+    kh::plan_compile(c, plan, p->cp);
+    const int64_t rows = int64_t(p->cp.length) * p->cp.batch;
+    kh::exec_alloc(p->ex, c, &p->cp, rows, p->cp.batch);
+  });
+  if (st != KH_OK) return st;
+  *out = p.release();
+  return KH_OK;
+}
+
+int kh_plan_info(const kh_plan* plan, int* length, int* batch, int* out_rows, int* out_cols, int64_t* bytes) {
+  if (!plan) {
+    g_err = "kh_plan_info: null plan";
+    return KH_ERR_ARG;
+  }
+  if (length) *length = plan->cp.length;
+  if (batch) *batch = plan->cp.batch;
+  if (out_rows) *out_rows = plan->cp.out_rows;
+  if (out_cols) *out_cols = plan->cp.out_cols;
+  if (bytes) *bytes = plan->ex.bytes;
+  return KH_OK;
+}
+
+int kh_upload(kh_plan* plan, const void* emb, size_t emb_bytes, const float* mask, size_t mask_len,
+              const uint32_t* type_ids, size_t type_len) {
+  if (!plan || !emb || !mask) {
+    g_err = "kh_upload: plan, embeddings and mask are required";
+    return KH_ERR_ARG;
+  }
+  Ctx* c = plan->owner->c.get();
+  return guard(c, Latch::Yes, [&] {
+    const kh::CompiledPlan& cp = plan->cp;
+    const int64_t rows = int64_t(cp.length) * cp.batch;
+    const size_t esz = cp.f16 ? 2 : 4;
+    if (emb_bytes > size_t(rows) * cp.emb_size * esz)
+      throw kh::ArgError("kh_upload: embeddings of " + std::to_string(emb_bytes) + " B exceed the plan's " +
+                         std::to_string(size_t(rows) * cp.emb_size * esz) + " B");
+    if (mask_len > size_t(rows)) throw kh::ArgError("kh_upload: mask longer than the plan rows");
+    KH_CUDA(cudaMemcpyAsync(plan->ex.buf(cp.buf_index.at(cp.in_emb)), emb, emb_bytes, cudaMemcpyHostToDevice,
+                            c->stream));
+    KH_CUDA(cudaMemcpyAsync(plan->ex.buf(cp.buf_index.at(cp.in_mask)), mask, mask_len * 4, cudaMemcpyHostToDevice,
+                            c->stream));
+    if (!cp.in_type.empty()) {
+      if (!type_ids) throw kh::ArgError("plan needs typeIds");
+      if (type_len > size_t(rows)) throw kh::ArgError("kh_upload: typeIds longer than the plan rows");
+      KH_CUDA(cudaMemcpyAsync(plan->ex.buf(cp.buf_index.at(cp.in_type)), type_ids, type_len * 4,
+                              cudaMemcpyHostToDevice, c->stream));
+    }
+    KH_CUDA(cudaStreamSynchronize(c->stream));  // the caller may reuse its arrays at once
+  });
+}
+
+static void plan_prepare(kh_plan* plan, int rows) {
+  const kh::CompiledPlan& cp = plan->cp;
+  const int L = cp.length, B = cp.batch;
+  if (rows < 1 || rows > L * B)
+    throw kh::ArgError("kh_run: " + std::to_string(rows) + " rows, the plan has " + std::to_string(L * B));
+  std::vector<int32_t> lens;
+  if (B == 1) lens.push_back(rows);
+  else
+    for (int b = 0; b < B; ++b) lens.push_back(std::max(0, std::min(L, rows - b * L)));
+  kh::SeqTable offs;
+  int64_t T = 0;
+  kh::build_seq_table(lens, cp.tile_q, plan->htable, offs, T);
+  kh::Exec& ex = plan->ex;
+  const int64_t words = int64_t(plan->htable.size());
+  if (words > ex.table_cap) {
+    if (ex.d_table) cudaFree(ex.d_table);
+    ex.d_table = nullptr;
+    KH_CUDA(cudaMalloc((void**)&ex.d_table, size_t(std::max<int64_t>(words, 1024)) * 4));
+    ex.table_cap = std::max<int64_t>(words, 1024);
+  }
+  KH_CUDA(cudaMemcpyAsync(ex.d_table, plan->htable.data(), size_t(words) * 4, cudaMemcpyHostToDevice,
+                          plan->owner->c->stream));
+  ex.seq = rebase(offs, ex.d_table);
+  ex.row_seq = ex.d_table + (intptr_t)offs.row_pos + T;
+  ex.T = int(T);
+}
+
+int kh_run(kh_plan* plan, int rows) {
+  if (!plan) {
+    g_err = "kh_run: null plan";
+    return KH_ERR_ARG;
+  }
+  Ctx* c = plan->owner->c.get();
+  return guard(c, Latch::Yes, [&] {
+    plan_prepare(plan, rows);
+    kh::exec_steps(plan->ex, c->stream);
+    const kh::CompiledPlan& cp = plan->cp;
+    kh::exec_output(plan->ex, cp.out_rows, plan->ex.d_out, c->stream);
+    KH_CUDA(cudaGetLastError());
+  });
+}
+
+int kh_read_output(kh_plan* plan, float* out, size_t n) {
+  if (!plan || !out) {
+    g_err = "kh_read_output: null argument";
+    return KH_ERR_ARG;
+  }
+  Ctx* c = plan->owner->c.get();
+  return guard(c, Latch::Yes, [&] {
+    const size_t need = size_t(plan->cp.out_rows) * plan->cp.out_cols;
+    if (n < need) throw kh::ArgError("kh_read_output: room for " + std::to_string(n) + " values, the output has " +
+                                     std::to_string(need));
+    KH_CUDA(cudaMemcpyAsync(out, plan->ex.d_out, need * 4, cudaMemcpyDeviceToHost, c->stream));
+    KH_CUDA(cudaStreamSynchronize(c->stream));
+  });
+}
+
+void kh_plan_destroy(kh_plan* plan) {
+  if (!plan) return;
+  cudaSetDevice(plan->owner->c->device);
+  cudaStreamSynchronize(plan->owner->c->stream);
+  delete plan;
+}
+
+void kh_destroy(kh_ctx* ctx) {
+  if (!ctx) return;
+  cudaSetDevice(ctx->c->device);
+  cudaStreamSynchronize(ctx->c->stream);
+  delete ctx;
+}
+
+size_t kh_info(const kh_ctx* ctx, char* buf, size_t cap) {
+  std::ostringstream o;
+  if (!ctx) return put_string("{}", buf, cap);
+  cudaDeviceProp prop;
+  std::string name = "?";
+  size_t total = 0;
+  if (cudaGetDeviceProperties(&prop, ctx->c->device) == cudaSuccess) {
+    name = prop.name;
+    total = prop.totalGlobalMem;
+  }
+  o << "{\"backend\":\"cuda\",\"device\":" << ctx->c->device << ",\"name\":\"" << json_escape(name)
+    << "\",\"sms\":" << ctx->c->sms << ",\"memoryBytes\":" << total << ",\"weightBytes\":" << ctx->c->weight_bytes
+    << ",\"broken\":\"" << json_escape(ctx->c->broken) << "\"}";
+  return put_string(o.str(), buf, cap);
+}
+
+size_t kh_plan_launches(const kh_plan* plan, char* buf, size_t cap) {
+  std::ostringstream o;
+  o << "[";
+  if (plan) {
+    bool first = true;
+    for (const kh::Step& s : plan->cp.steps) {
+      if (!first) o << ",";
+      first = false;
+      o << "{\"label\":\"" << json_escape(s.label) << "\",\"launches\":" << s.launches << ",\"ops\":[";
+      for (size_t i = 0; i < s.ops.size(); ++i) o << (i ? "," : "") << "\"" << json_escape(s.ops[i]) << "\"";
+      o << "]}";
+    }
+    o << (first ? "" : ",") << "{\"label\":\"output\",\"launches\":1,\"ops\":[]}";
+  }
+  o << "]";
+  return put_string(o.str(), buf, cap);
+}
+
+int kh_profile(kh_plan* plan, int rows, float* ms, size_t n) {
+  if (!plan || (n && !ms)) {
+    g_err = "kh_profile: null argument";
+    return KH_ERR_ARG;
+  }
+  Ctx* c = plan->owner->c.get();
+  return guard(c, Latch::Yes, [&] {
+    plan_prepare(plan, rows);
+    const auto& steps = plan->cp.steps;
+    std::vector<cudaEvent_t> ev(steps.size() + 2);
+    for (auto& e : ev) KH_CUDA(cudaEventCreate(&e));
+    KH_CUDA(cudaEventRecord(ev[0], c->stream));
+    for (size_t i = 0; i < steps.size(); ++i) {
+      steps[i].run(plan->ex, c->stream);
+      KH_CUDA(cudaEventRecord(ev[i + 1], c->stream));
+    }
+    kh::exec_output(plan->ex, plan->cp.out_rows, plan->ex.d_out, c->stream);
+    KH_CUDA(cudaEventRecord(ev[steps.size() + 1], c->stream));
+    KH_CUDA(cudaGetLastError());
+    KH_CUDA(cudaEventSynchronize(ev.back()));
+    for (size_t i = 0; i + 1 < ev.size() && i < n; ++i) KH_CUDA(cudaEventElapsedTime(&ms[i], ev[i], ev[i + 1]));
+    for (auto& e : ev) cudaEventDestroy(e);
+  });
+}
+
+int kh_bulk_create(kh_plan* plan, int64_t max_tokens, int max_seqs, int64_t chunk_tokens, kh_bulk** out) {
+  if (!plan || !out) {
+    g_err = "kh_bulk_create: null argument";
+    return KH_ERR_ARG;
+  }
+  *out = nullptr;
+  Ctx* c = plan->owner->c.get();
+  auto b = std::make_unique<kh_bulk>();
+  b->plan = plan;
+  const int st = guard(c, Latch::No, [&] {
+    const kh::CompiledPlan& cp = plan->cp;
+    if (max_tokens < 1 || max_seqs < 1) throw kh::ArgError("kh_bulk_create: max_tokens and max_seqs must be >= 1");
+    if (chunk_tokens < cp.length)
+      throw kh::ArgError("kh_bulk_create: chunk_tokens " + std::to_string(chunk_tokens) +
+                         " below the plan length " + std::to_string(cp.length));
+    chunk_tokens = std::min(chunk_tokens, std::max<int64_t>(max_tokens, cp.length));
+    b->max_tokens = max_tokens;
+    b->max_seqs = max_seqs;
+    b->chunk_tokens = chunk_tokens;
+    const int cap_seqs = int(std::min<int64_t>(max_seqs, chunk_tokens));
+    kh::exec_alloc(b->ex, c, &cp, chunk_tokens, cap_seqs);
+    const size_t esz = cp.f16 ? 2 : 4;
+    KH_CUDA(cudaMalloc(&b->d_emb, size_t(max_tokens) * cp.emb_size * esz + 256));
+    if (!cp.in_type.empty()) KH_CUDA(cudaMalloc((void**)&b->d_type, size_t(max_tokens) * 4 + 256));
+    KH_CUDA(cudaMalloc((void**)&b->d_mask, size_t(max_tokens) * 4 + 256));
+    std::vector<float> ones(size_t(max_tokens), 1.0f);
+    KH_CUDA(cudaMemcpy(b->d_mask, ones.data(), size_t(max_tokens) * 4, cudaMemcpyHostToDevice));
+    const int64_t out_rows = cp.out_per_seq ? max_seqs : max_tokens;
+    KH_CUDA(cudaMalloc((void**)&b->d_out, size_t(out_rows) * cp.out_cols * 4 + 256));
+    KH_CUDA(cudaEventCreate(&b->ev0));
+    KH_CUDA(cudaEventCreate(&b->ev1));
+  });
+  if (st != KH_OK) return st;
+  *out = b.release();
+  return KH_OK;
+}
+
+int kh_bulk_set_lengths(kh_bulk* bulk, const int32_t* seq_lens, int n) {
+  if (!bulk || (n > 0 && !seq_lens)) {
+    g_err = "kh_bulk_set_lengths: null argument";
+    return KH_ERR_ARG;
+  }
+  Ctx* c = bulk->plan->owner->c.get();
+  return guard(c, Latch::Yes, [&] {
+    const kh::CompiledPlan& cp = bulk->plan->cp;
+    if (n < 1 || n > bulk->max_seqs)
+      throw kh::ArgError("kh_bulk_set_lengths: " + std::to_string(n) + " sequences, room for " +
+                         std::to_string(bulk->max_seqs));
+    int64_t total = 0;
+    for (int i = 0; i < n; ++i) {
+      if (seq_lens[i] < 1 || seq_lens[i] > cp.length)
+        throw kh::ArgError("kh_bulk_set_lengths: sequence " + std::to_string(i) + " has " +
+                           std::to_string(seq_lens[i]) + " rows, the plan takes 1 to " + std::to_string(cp.length));
+      total += seq_lens[i];
+    }
+    if (total > bulk->max_tokens)
+      throw kh::ArgError("kh_bulk_set_lengths: " + std::to_string(total) + " rows, room for " +
+                         std::to_string(bulk->max_tokens));
+    bulk->chunks.clear();
+    std::vector<int32_t> all;
+    int s = 0;
+    int64_t tok = 0;
+    const int cap_seqs = bulk->ex.cap_seqs;
+    while (s < n) {
+      kh_bulk::Chunk ch;
+      ch.seq0 = s;
+      ch.tok0 = tok;
+      std::vector<int32_t> lens;
+      int64_t T = 0;
+      while (s < n && T + seq_lens[s] <= bulk->chunk_tokens && int(lens.size()) < cap_seqs) {
+        lens.push_back(seq_lens[s]);
+        T += seq_lens[s];
+        ++s;
+      }
+      std::vector<int32_t> table;
+      int64_t t2 = 0;
+      kh::build_seq_table(lens, cp.tile_q, table, ch.seq, t2);
+      ch.T = T;
+      ch.S = int(lens.size());
+      ch.word0 = int64_t(all.size());
+      all.insert(all.end(), table.begin(), table.end());
+      bulk->chunks.push_back(ch);
+      tok += T;
+    }
+    const int64_t words = int64_t(all.size());
+    if (words > bulk->table_cap) {
+      cudaFree(bulk->d_table);
+      bulk->d_table = nullptr;
+      KH_CUDA(cudaMalloc((void**)&bulk->d_table, size_t(words) * 4));
+      bulk->table_cap = words;
+    }
+    KH_CUDA(cudaMemcpy(bulk->d_table, all.data(), size_t(words) * 4, cudaMemcpyHostToDevice));
+    bulk->n_seqs = n;
+    bulk->n_tokens = total;
+  });
+}
+
+int kh_bulk_upload(kh_bulk* bulk, const void* emb, size_t emb_bytes, const uint32_t* type_ids, size_t type_len) {
+  if (!bulk || !emb) {
+    g_err = "kh_bulk_upload: bulk and embeddings are required";
+    return KH_ERR_ARG;
+  }
+  Ctx* c = bulk->plan->owner->c.get();
+  return guard(c, Latch::Yes, [&] {
+    const kh::CompiledPlan& cp = bulk->plan->cp;
+    const size_t need = size_t(bulk->n_tokens) * cp.emb_size * (cp.f16 ? 2 : 4);
+    if (emb_bytes != need)
+      throw kh::ArgError("kh_bulk_upload: embeddings of " + std::to_string(emb_bytes) + " B, the sequences need " +
+                         std::to_string(need));
+    KH_CUDA(cudaMemcpyAsync(bulk->d_emb, emb, need, cudaMemcpyHostToDevice, c->stream));
+    if (!cp.in_type.empty()) {
+      if (!type_ids || type_len != size_t(bulk->n_tokens)) throw kh::ArgError("plan needs typeIds for every row");
+      KH_CUDA(cudaMemcpyAsync(bulk->d_type, type_ids, type_len * 4, cudaMemcpyHostToDevice, c->stream));
+    }
+  });
+}
+
+int kh_bulk_run(kh_bulk* bulk) {
+  if (!bulk) {
+    g_err = "kh_bulk_run: null bulk";
+    return KH_ERR_ARG;
+  }
+  Ctx* c = bulk->plan->owner->c.get();
+  return guard(c, Latch::Yes, [&] {
+    const kh::CompiledPlan& cp = bulk->plan->cp;
+    kh::Exec& ex = bulk->ex;
+    const size_t esz = cp.f16 ? 2 : 4;
+    const int ie = cp.buf_index.at(cp.in_emb), im = cp.buf_index.at(cp.in_mask);
+    const int it = cp.in_type.empty() ? -1 : cp.buf_index.at(cp.in_type);
+    int64_t launches = 0;
+    int64_t per_chunk = 1;
+    for (const kh::Step& s : cp.steps) per_chunk += s.launches;
+    KH_CUDA(cudaEventRecord(bulk->ev0, c->stream));
+    for (const kh_bulk::Chunk& ch : bulk->chunks) {
+      ex.ptr[ie] = (char*)bulk->d_emb + size_t(ch.tok0) * cp.emb_size * esz;
+      ex.ptr[im] = bulk->d_mask + ch.tok0;
+      if (it >= 0) ex.ptr[it] = bulk->d_type + ch.tok0;
+      const int32_t* base = bulk->d_table + ch.word0;
+      ex.seq = rebase(ch.seq, base);
+      ex.row_seq = const_cast<int32_t*>(base) + (intptr_t)ch.seq.row_pos + ch.T;
+      ex.T = int(ch.T);
+      kh::exec_steps(ex, c->stream);
+      float* dst = bulk->d_out + (cp.out_per_seq ? int64_t(ch.seq0) : ch.tok0) * cp.out_cols;
+      kh::exec_output(ex, cp.out_per_seq ? ch.S : int(ch.T), dst, c->stream);
+      launches += per_chunk;
+    }
+    KH_CUDA(cudaEventRecord(bulk->ev1, c->stream));
+    KH_CUDA(cudaGetLastError());
+    bulk->last_launches = launches;
+  });
+}
+
+int kh_bulk_read(kh_bulk* bulk, float* out, size_t n) {
+  if (!bulk || !out) {
+    g_err = "kh_bulk_read: null argument";
+    return KH_ERR_ARG;
+  }
+  Ctx* c = bulk->plan->owner->c.get();
+  return guard(c, Latch::Yes, [&] {
+    const kh::CompiledPlan& cp = bulk->plan->cp;
+    const size_t need = size_t(cp.out_per_seq ? bulk->n_seqs : bulk->n_tokens) * cp.out_cols;
+    if (n < need) throw kh::ArgError("kh_bulk_read: room for " + std::to_string(n) + " values, the output has " +
+                                     std::to_string(need));
+    KH_CUDA(cudaMemcpyAsync(out, bulk->d_out, need * 4, cudaMemcpyDeviceToHost, c->stream));
+    KH_CUDA(cudaStreamSynchronize(c->stream));
+  });
+}
+
+int kh_run_batch(kh_bulk* bulk, const int32_t* seq_lens, int n, const void* emb, size_t emb_bytes,
+                 const uint32_t* type_ids, size_t type_len, float* out, size_t out_len) {
+  int st = kh_bulk_set_lengths(bulk, seq_lens, n);
+  if (st == KH_OK) st = kh_bulk_upload(bulk, emb, emb_bytes, type_ids, type_len);
+  if (st == KH_OK) st = kh_bulk_run(bulk);
+  if (st == KH_OK) st = kh_bulk_read(bulk, out, out_len);
+  return st;
+}
+
+int kh_bulk_last_timing(const kh_bulk* bulk, float* ms, int64_t* launches) {
+  if (!bulk) {
+    g_err = "kh_bulk_last_timing: null bulk";
+    return KH_ERR_ARG;
+  }
+  Ctx* c = bulk->plan->owner->c.get();
+  return guard(c, Latch::Yes, [&] {
+    KH_CUDA(cudaEventSynchronize(bulk->ev1));
+    if (ms) KH_CUDA(cudaEventElapsedTime(ms, bulk->ev0, bulk->ev1));
+    if (launches) *launches = bulk->last_launches;
+  });
+}
+
+void kh_bulk_destroy(kh_bulk* bulk) {
+  if (!bulk) return;
+  cudaSetDevice(bulk->plan->owner->c->device);
+  cudaStreamSynchronize(bulk->plan->owner->c->stream);
+  delete bulk;
+}
+
+}  // extern "C"

@@ -1,0 +1,489 @@
+// Row kernels of the plan (bandwidth-bound) and the CUDA-core fallbacks of the contractions.
+// Storage type T is __half for f16 plans and float for f32 plans; every kernel computes in f32
+// and rounds once on store, as the reference kernels do (src/kernels/index.ts:1-3).
+//
+// Reference semantics per kernel are cited at each launcher. Row kernels use one warp per row
+// with the row held in registers between the two LayerNorm passes (the variance is the mean of
+// (v - mean)^2, src/kernels/layernorm.wgsl:18-20).
+
+#include "kernels.h"
+
+#include <cmath>
+#include <cstdio>
+#include <stdexcept>
+
+namespace kh {
+
+namespace {
+
+template <typename T> __device__ __forceinline__ float ld(const T* p, int64_t i);
+template <> __device__ __forceinline__ float ld<float>(const float* p, int64_t i) { return p[i]; }
+template <> __device__ __forceinline__ float ld<__half>(const __half* p, int64_t i) { return __half2float(p[i]); }
+template <typename T> __device__ __forceinline__ void st(T* p, int64_t i, float v);
+template <> __device__ __forceinline__ void st<float>(float* p, int64_t i, float v) { p[i] = v; }
+template <> __device__ __forceinline__ void st<__half>(__half* p, int64_t i, float v) { p[i] = __float2half_rn(v); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// GELU with the Abramowitz-Stegun 7.1.26 erf (src/kernels/mmtile.wgsl:22-31, the constants the
+// reference prints); exp through CUDA's expf.
+__device__ __forceinline__ float gelu_as(float v) {
+  const float u = v * 0.7071067811865476f;
+  const float t = 1.0f / (1.0f + 0.3275911f * fabsf(u));
+  const float p = (((((1.061405429f * t - 1.453152027f) * t) + 1.421413741f) * t - 0.284496736f) * t +
+                   0.254829592f) * t;
+  const float e = 1.0f - p * expf(-u * u);
+  return 0.5f * v * (1.0f + (v >= 0.0f ? e : -e));
+}
+
+__device__ __forceinline__ float activate(float v, int act) {
+  if (act == 1) return fmaxf(v, 0.0f);
+  if (act == 2) return gelu_as(v);
+  if (act == 3) return tanhf(v);
+  if (act == 4) return v / (1.0f + expf(-v));
+  return v;
+}
+
+constexpr int MAXE = 32;  // elements per lane held in registers: N <= 1024
+
+// Two-pass LayerNorm over a row held as v[k] = x[lane + 32 k], k < n_per_lane.
+__device__ __forceinline__ void ln_stats(const float* v, int N, float eps, float& mean, float& inv) {
+  const int lane = threadIdx.x & 31;
+  float s = 0.f;
+#pragma unroll
+  for (int k = 0; k < MAXE; ++k) {
+    const int d = lane + 32 * k;
+    if (d < N) s += v[k];
+  }
+  mean = warp_sum(s) / float(N);
+  float q = 0.f;
+#pragma unroll
+  for (int k = 0; k < MAXE; ++k) {
+    const int d = lane + 32 * k;
+    if (d < N) {
+      const float x = v[k] - mean;
+      q += x * x;
+    }
+  }
+  const float var = warp_sum(q) / float(N);
+  inv = 1.0f / sqrtf(var + eps);
+}
+
+template <typename T>
+__global__ void embln_kernel(const T* __restrict__ word, const T* __restrict__ pos, const T* __restrict__ typ,
+                             const uint32_t* __restrict__ tt, const T* __restrict__ w, const T* __restrict__ b,
+                             const float* __restrict__ mask, T* __restrict__ out, int N, int rows,
+                             const int32_t* __restrict__ row_pos, int offset, int maxpos, float eps, int maskmul,
+                             int posids) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int lane = threadIdx.x & 31;
+  const uint32_t t = tt ? tt[row] : 0u;
+  int prow = posids ? int(t >> 16) : row_pos[row] + offset;
+  prow = min(prow, maxpos - 1);
+  const int64_t wbase = int64_t(row) * N, pbase = int64_t(prow) * N, tbase = int64_t(t & 0xffffu) * N;
+  float v[MAXE];
+#pragma unroll
+  for (int k = 0; k < MAXE; ++k) {
+    const int d = lane + 32 * k;
+    v[k] = d < N ? ld(word, wbase + d) + ld(pos, pbase + d) + ld(typ, tbase + d) : 0.f;
+  }
+  float mean, inv;
+  ln_stats(v, N, eps, mean, inv);
+  const float m = maskmul ? mask[row] : 1.0f;
+#pragma unroll
+  for (int k = 0; k < MAXE; ++k) {
+    const int d = lane + 32 * k;
+    if (d < N) {
+      float y = (v[k] - mean) * inv * ld(w, d) + ld(b, d);
+      if (maskmul) y *= m;
+      st(out, wbase + d, y);
+    }
+  }
+}
+
+template <typename T>
+__global__ void layernorm_kernel(const T* __restrict__ a, const T* __restrict__ bb, const T* __restrict__ w,
+                                 const T* __restrict__ bias, const float* __restrict__ mask, T* __restrict__ out,
+                                 int N, int rows, int mode, float eps) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int lane = threadIdx.x & 31;
+  const int64_t base = int64_t(row) * N;
+  float v[MAXE];
+#pragma unroll
+  for (int k = 0; k < MAXE; ++k) {
+    const int d = lane + 32 * k;
+    float x = 0.f;
+    if (d < N) {
+      x = ld(a, base + d);
+      if (mode == 2) x += ld(bb, base + d);
+    }
+    v[k] = x;
+  }
+  float mean, inv;
+  ln_stats(v, N, eps, mean, inv);
+  const float m = mode == 1 ? mask[row] : 1.0f;
+#pragma unroll
+  for (int k = 0; k < MAXE; ++k) {
+    const int d = lane + 32 * k;
+    if (d < N) {
+      float y = (v[k] - mean) * inv * ld(w, d) + ld(bias, d);
+      if (mode == 1) y *= m;
+      st(out, base + d, y);
+    }
+  }
+}
+
+template <typename T>
+__global__ void add_kernel(T* __restrict__ dst, const T* __restrict__ src, int64_t count) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < count; i += int64_t(gridDim.x) * blockDim.x)
+    st(dst, i, ld(dst, i) + ld(src, i));
+}
+
+template <typename T>
+__global__ void geglu_kernel(const T* __restrict__ mid, T* __restrict__ gate, int I, int rows) {
+  const int64_t total = int64_t(rows) * I;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = i / I;
+    const int j = int(i - r * I);
+    st(gate, i, gelu_as(ld(mid, r * 2 * I + j)) * ld(mid, r * 2 * I + I + j));
+  }
+}
+
+template <typename T>
+__global__ void rope_kernel(T* __restrict__ qkv, const float* __restrict__ cossin, const int32_t* __restrict__ row_pos,
+                            int H, int D, int rows) {
+  const int half = D / 2;
+  const int64_t total = int64_t(rows) * 2 * H * half;
+  for (int64_t idx = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; idx < total;
+       idx += int64_t(gridDim.x) * blockDim.x) {
+    const int d = int(idx % half);
+    const int64_t rs = idx / half;
+    const int s = int(rs % (2 * H));
+    const int64_t i = rs / (2 * H);
+    const int il = row_pos[i];
+    const int64_t base = i * 3 * H * D + int64_t(s) * D;
+    const float a = ld(qkv, base + d), b = ld(qkv, base + d + half);
+    const float c = cossin[int64_t(il) * 2 * D + d], sn = cossin[int64_t(il) * 2 * D + D + d];
+    st(qkv, base + d, a * c - b * sn);
+    st(qkv, base + d + half, b * c + a * sn);
+  }
+}
+
+template <typename T>
+__global__ void pool_kernel(const T* __restrict__ x, const float* __restrict__ mask, T* __restrict__ out, int N,
+                            int mode, const int32_t* __restrict__ start, const int32_t* __restrict__ len) {
+  const int s = blockIdx.y;
+  const int d = blockIdx.x * blockDim.x + threadIdx.x;
+  if (d >= N) return;
+  const int r0 = start[s], n = len[s];
+  if (mode == 0) {
+    float acc = 0.f, cnt = 0.f;
+    for (int i = 0; i < n; ++i) {
+      const float m = mask[r0 + i];
+      if (m != 0.f) {
+        acc += m * ld(x, int64_t(r0 + i) * N + d);
+        cnt += m;
+      }
+    }
+    st(out, int64_t(s) * N + d, acc / fmaxf(cnt, 1e-9f));
+  } else {
+    float best = 0.f;
+    bool found = false;
+    for (int i = 0; i < n; ++i) {
+      if (mask[r0 + i] > 0.5f) {
+        const float v = ld(x, int64_t(r0 + i) * N + d);
+        best = found ? fmaxf(best, v) : v;
+        found = true;
+      }
+    }
+    st(out, int64_t(s) * N + d, best);
+  }
+}
+
+template <typename T>
+__global__ void gather_kernel(const T* __restrict__ x, T* __restrict__ out, int D, const int32_t* __restrict__ start,
+                              const uint32_t* __restrict__ markers, int K, int S) {
+  const int g = blockIdx.x;  // output row
+  const int s = g / K;
+  if (s >= S) return;
+  const int local = markers ? int(markers[s * 3 * K + (g - s * K)]) : 0;
+  const int64_t row = int64_t(start[s]) + local;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) st(out, int64_t(g) * D + d, ld(x, row * D + d));
+}
+
+template <typename T>
+__global__ void im2col_kernel(const T* __restrict__ x, const float* __restrict__ mask, T* __restrict__ out, int N,
+                              int KS, int rows, const int32_t* __restrict__ start, const int32_t* __restrict__ len,
+                              const int32_t* __restrict__ row_seq, const int32_t* __restrict__ row_pos) {
+  const int r = blockIdx.x;
+  if (r >= rows) return;
+  const int s = row_seq[r], i = row_pos[r], L = len[s], base = start[s];
+  const int pad = (KS - 1) / 2;
+  for (int t = 0; t < KS; ++t) {
+    const int j = i + t - pad;
+    const int src = base + max(j, 0);
+    const bool ok = j >= 0 && j < L && mask[src] != 0.f;
+    for (int c = threadIdx.x; c < N; c += blockDim.x)
+      st(out, int64_t(r) * KS * N + int64_t(t) * N + c, ok ? ld(x, int64_t(src) * N + c) : 0.f);
+  }
+}
+
+// C = act(A W^T + bias): 64 x 64 tiles, 256 threads with 4 x 4 outputs, k in steps of 16.
+template <typename T>
+__global__ void __launch_bounds__(256) gemm_simt_kernel(const T* __restrict__ A, const T* __restrict__ W,
+                                                        const T* __restrict__ bias, T* __restrict__ C, int M, int N,
+                                                        int K, int act) {
+  __shared__ float sa[16][64 + 1];
+  __shared__ float sw[16][64 + 1];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < K; k0 += 16) {
+    for (int e = threadIdx.x; e < 64 * 16; e += 256) {
+      const int r = e / 16, kk = e % 16;
+      const int gm = m0 + r, gn = n0 + r, gk = k0 + kk;
+      sa[kk][r] = (gm < M && gk < K) ? ld(A, int64_t(gm) * K + gk) : 0.f;
+      sw[kk][r] = (gn < N && gk < K) ? ld(W, int64_t(gn) * K + gk) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = sa[kk][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = sw[kk][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int gm = m0 + ty * 4 + i;
+    if (gm >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int gn = n0 + tx * 4 + j;
+      if (gn < N) st(C, int64_t(gm) * N + gn, activate(acc[i][j] + (bias ? ld(bias, gn) : 0.f), act));
+    }
+  }
+}
+
+// Attention on CUDA cores, flash form: one thread per query row (64 rows per CTA, one head),
+// keys in chunks of 32 through shared memory, online softmax in f32.
+constexpr int AQ = 64;
+constexpr int AK = 32;
+
+template <typename T>
+__global__ void __launch_bounds__(AQ) attention_simt_kernel(AttnArgs a, SeqTable seq) {
+  const int tile = blockIdx.x;
+  const int h = blockIdx.y;
+  const int s = seq.tiles[2 * tile], q0 = seq.tiles[2 * tile + 1];
+  const int base = seq.start[s], n = seq.len[s];
+  const int H = a.H, D = a.D, hd = H * D;
+  const T* qkv = static_cast<const T*>(a.qkv);
+  T* ctx = static_cast<T*>(a.ctx);
+  __shared__ float sk[AK][64 + 1];
+  __shared__ float sv[AK][64 + 1];
+  __shared__ float skm[AK];
+  const int i = q0 + threadIdx.x;  // local query
+  const bool active = i < n;
+  const int64_t qrow = int64_t(base) + i;
+  float q[64];
+  float acc[64];
+#pragma unroll
+  for (int d = 0; d < 64; ++d) {
+    q[d] = (active && d < D) ? ld(qkv, qrow * 3 * hd + int64_t(h) * D + d) : 0.f;
+    acc[d] = 0.f;
+  }
+  const bool qvalid = active && a.mask[qrow] > 0.5f;
+  float m = -3.40282346638528859812e38f, l = 0.f;
+  const T* pk = static_cast<const T*>(a.pos_key);
+  const T* pq = static_cast<const T*>(a.pos_query);
+  for (int j0 = 0; j0 < n; j0 += AK) {
+    __syncthreads();
+    for (int e = threadIdx.x; e < AK * D; e += AQ) {
+      const int jj = e / D, d = e % D;
+      const int j = j0 + jj;
+      float kv = 0.f, vv = 0.f;
+      if (j < n) {
+        const int64_t kr = int64_t(base + j) * 3 * hd;
+        kv = ld(qkv, kr + int64_t(H + h) * D + d);
+        vv = ld(qkv, kr + int64_t(2 * H + h) * D + d);
+      }
+      sk[jj][d] = kv;
+      sv[jj][d] = vv;
+    }
+    for (int jj = threadIdx.x; jj < AK; jj += AQ) {
+      const int j = j0 + jj;
+      skm[jj] = (j < n && a.mask[base + j] > 0.5f) ? 1.f : 0.f;
+    }
+    __syncthreads();
+    if (!qvalid) continue;
+    for (int jj = 0; jj < AK; ++jj) {
+      const int j = j0 + jj;
+      if (j >= n || skm[jj] == 0.f) continue;
+      if (a.window && abs(i - j) > a.window) continue;
+      float sc = 0.f;
+#pragma unroll
+      for (int d = 0; d < 64; ++d)
+        if (d < D) sc += q[d] * sk[jj][d];
+      if (a.rel) {
+        const int64_t p = a.relidx[int64_t(i) * a.L + j];
+        float c2p = 0.f, p2c = 0.f;
+        for (int d = 0; d < D; ++d) {
+          c2p += q[d] * ld(pk, p * hd + int64_t(h) * D + d);
+          p2c += sk[jj][d] * ld(pq, p * hd + int64_t(h) * D + d);
+        }
+        sc = (sc + c2p + p2c) * a.scale;
+      } else {
+        sc *= a.scale;
+      }
+      const float mn = fmaxf(m, sc);
+      const float corr = expf(m - mn);
+      const float pexp = expf(sc - mn);
+      l = l * corr + pexp;
+#pragma unroll
+      for (int d = 0; d < 64; ++d)
+        if (d < D) acc[d] = acc[d] * corr + pexp * sv[jj][d];
+      m = mn;
+    }
+  }
+  if (!active) return;
+  const float invl = (qvalid && l > 0.f) ? 1.0f / l : 0.f;
+#pragma unroll
+  for (int d = 0; d < 64; ++d)
+    if (d < D) st(ctx, qrow * hd + int64_t(h) * D + d, acc[d] * invl);
+}
+
+__global__ void f32_to_f16_kernel(const float* src, __half* dst, int64_t n) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
+    dst[i] = __float2half_rn(src[i]);
+}
+__global__ void f16_to_f32_kernel(const __half* src, float* dst, int64_t n) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
+    dst[i] = __half2float(src[i]);
+}
+
+inline int grid_for(int64_t n, int threads) {
+  int64_t g = (n + threads - 1) / threads;
+  if (g > 148 * 32) g = 148 * 32;
+  return int(g < 1 ? 1 : g);
+}
+
+}  // namespace
+
+void launch_embln(bool f16, const void* word, const void* pos, const void* typ, const uint32_t* tt, const void* w,
+                  const void* b, const float* mask, void* out, int N, int rows, const int32_t* row_pos, int offset,
+                  int maxpos, float eps, int maskmul, int posids, cudaStream_t st) {
+  if (N > 32 * MAXE) throw std::runtime_error("embln: width above 1024");
+  if (rows <= 0) return;
+  const int grid = (rows + 7) / 8;
+  if (f16)
+    embln_kernel<__half><<<grid, 256, 0, st>>>((const __half*)word, (const __half*)pos, (const __half*)typ, tt,
+                                               (const __half*)w, (const __half*)b, mask, (__half*)out, N, rows,
+                                               row_pos, offset, maxpos, eps, maskmul, posids);
+  else
+    embln_kernel<float><<<grid, 256, 0, st>>>((const float*)word, (const float*)pos, (const float*)typ, tt,
+                                              (const float*)w, (const float*)b, mask, (float*)out, N, rows, row_pos,
+                                              offset, maxpos, eps, maskmul, posids);
+}
+
+void launch_layernorm(bool f16, const void* a, const void* b, const void* w, const void* bias, const float* mask,
+                      void* out, int N, int rows, int mode, float eps, cudaStream_t st) {
+  if (N > 32 * MAXE) throw std::runtime_error("layernorm: width above 1024");
+  if (rows <= 0) return;
+  const int grid = (rows + 7) / 8;
+  if (f16)
+    layernorm_kernel<__half><<<grid, 256, 0, st>>>((const __half*)a, (const __half*)b, (const __half*)w,
+                                                   (const __half*)bias, mask, (__half*)out, N, rows, mode, eps);
+  else
+    layernorm_kernel<float><<<grid, 256, 0, st>>>((const float*)a, (const float*)b, (const float*)w,
+                                                  (const float*)bias, mask, (float*)out, N, rows, mode, eps);
+}
+
+void launch_add(bool f16, void* dst, const void* src, int64_t count, cudaStream_t st) {
+  if (count <= 0) return;
+  if (f16) add_kernel<__half><<<grid_for(count, 256), 256, 0, st>>>((__half*)dst, (const __half*)src, count);
+  else add_kernel<float><<<grid_for(count, 256), 256, 0, st>>>((float*)dst, (const float*)src, count);
+}
+
+void launch_geglu(bool f16, const void* mid, void* gate, int I, int rows, cudaStream_t st) {
+  const int64_t n = int64_t(rows) * I;
+  if (n <= 0) return;
+  if (f16) geglu_kernel<__half><<<grid_for(n, 256), 256, 0, st>>>((const __half*)mid, (__half*)gate, I, rows);
+  else geglu_kernel<float><<<grid_for(n, 256), 256, 0, st>>>((const float*)mid, (float*)gate, I, rows);
+}
+
+void launch_rope(bool f16, void* qkv, const float* cossin, const int32_t* row_pos, int H, int D, int rows,
+                 cudaStream_t st) {
+  const int64_t n = int64_t(rows) * H * D;
+  if (n <= 0) return;
+  if (f16) rope_kernel<__half><<<grid_for(n, 256), 256, 0, st>>>((__half*)qkv, cossin, row_pos, H, D, rows);
+  else rope_kernel<float><<<grid_for(n, 256), 256, 0, st>>>((float*)qkv, cossin, row_pos, H, D, rows);
+}
+
+void launch_pool(bool f16, const void* x, const float* mask, void* out, int N, int mode, const SeqTable& seq,
+                 cudaStream_t st) {
+  if (seq.count <= 0) return;
+  dim3 grid((N + 127) / 128, seq.count);
+  if (f16) pool_kernel<__half><<<grid, 128, 0, st>>>((const __half*)x, mask, (__half*)out, N, mode, seq.start, seq.len);
+  else pool_kernel<float><<<grid, 128, 0, st>>>((const float*)x, mask, (float*)out, N, mode, seq.start, seq.len);
+}
+
+void launch_gather(bool f16, const void* x, void* out, int D, const SeqTable& seq, const uint32_t* markers, int K,
+                   cudaStream_t st) {
+  if (seq.count <= 0) return;
+  const int grid = seq.count * K;
+  if (f16) gather_kernel<__half><<<grid, 128, 0, st>>>((const __half*)x, (__half*)out, D, seq.start, markers, K, seq.count);
+  else gather_kernel<float><<<grid, 128, 0, st>>>((const float*)x, (float*)out, D, seq.start, markers, K, seq.count);
+}
+
+void launch_im2col(bool f16, const void* x, const float* mask, void* out, int N, int KS, int rows, const SeqTable& seq,
+                   const int32_t* row_seq, cudaStream_t st) {
+  if (rows <= 0) return;
+  if (f16)
+    im2col_kernel<__half><<<rows, 128, 0, st>>>((const __half*)x, mask, (__half*)out, N, KS, rows, seq.start, seq.len,
+                                                row_seq, seq.row_pos);
+  else
+    im2col_kernel<float><<<rows, 128, 0, st>>>((const float*)x, mask, (float*)out, N, KS, rows, seq.start, seq.len,
+                                               row_seq, seq.row_pos);
+}
+
+void launch_gemm_simt(bool f16, const void* A, const void* W, const void* bias, void* C, int M, int N, int K, int act,
+                      cudaStream_t st) {
+  if (M <= 0 || N <= 0) return;
+  dim3 grid((N + 63) / 64, (M + 63) / 64);
+  if (f16)
+    gemm_simt_kernel<__half><<<grid, 256, 0, st>>>((const __half*)A, (const __half*)W, (const __half*)bias,
+                                                   (__half*)C, M, N, K, act);
+  else
+    gemm_simt_kernel<float><<<grid, 256, 0, st>>>((const float*)A, (const float*)W, (const float*)bias, (float*)C, M,
+                                                  N, K, act);
+}
+
+void launch_attention_simt(bool f16, const AttnArgs& a, const SeqTable& seq, cudaStream_t st) {
+  if (a.D > 64) throw std::runtime_error("attention: head dimension above 64");
+  if (seq.ntiles <= 0) return;
+  dim3 grid(seq.ntiles, a.H);
+  if (f16) attention_simt_kernel<__half><<<grid, AQ, 0, st>>>(a, seq);
+  else attention_simt_kernel<float><<<grid, AQ, 0, st>>>(a, seq);
+}
+
+void launch_f32_to_f16(const float* src, __half* dst, int64_t n, cudaStream_t st) {
+  if (n > 0) f32_to_f16_kernel<<<grid_for(n, 256), 256, 0, st>>>(src, dst, n);
+}
+void launch_f16_to_f32(const __half* src, float* dst, int64_t n, cudaStream_t st) {
+  if (n > 0) f16_to_f32_kernel<<<grid_for(n, 256), 256, 0, st>>>(src, dst, n);
+}
+
+}  // namespace kh

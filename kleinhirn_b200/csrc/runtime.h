@@ -1,0 +1,125 @@
+// Host runtime of the CUDA backend: context, weights, compiled plans, executions.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <functional>
+#include <map>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "json.hpp"
+#include "kernels.h"
+
+namespace kh {
+
+struct CudaError : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+struct ArgError : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+struct PlanError : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+
+void cuda_check(cudaError_t e, const char* what);
+#define KH_CUDA(x) ::kh::cuda_check((x), #x)
+
+struct DevTensor {
+  std::string name;
+  int dtype = 0;  // 0 f32, 1 f16
+  std::vector<int64_t> shape;
+  void* ptr = nullptr;
+  size_t bytes = 0;
+  int64_t numel() const {
+    int64_t n = 1;
+    for (auto s : shape) n *= s;
+    return n;
+  }
+};
+
+struct Ctx {
+  int device = 0;
+  int sms = 0;
+  cudaStream_t stream = nullptr;
+  std::map<std::string, DevTensor> tensors;  // as added
+  std::map<std::string, DevTensor> derived;  // dtype conversions and repacked layouts
+  int64_t weight_bytes = 0;
+  std::string broken;  // first CUDA error of a run: latched (src/device.ts:79-81)
+  ~Ctx();
+  // The tensor in storage type f16 (true) or f32, converted once on the device and cached.
+  const DevTensor& weight(const std::string& name, bool f16);
+  // A derived tensor built by `make` once and cached under `key`.
+  const DevTensor& derive(const std::string& key, const std::function<DevTensor()>& make);
+};
+
+// One launch group of a compiled plan.
+struct Exec;
+struct Step {
+  std::string label;               // kernel family, e.g. "gemm_tc", "layernorm"
+  std::vector<std::string> ops;    // plan op names covered
+  int launches = 1;
+  std::function<void(Exec&, cudaStream_t)> run;
+};
+
+// Buffer of a plan: row buffers scale with the packed rows, sequence buffers with the
+// sequences of a launch, fixed buffers (init tables) keep their plan size.
+struct BufInfo {
+  std::string id;
+  enum Kind { Rows, Seqs, Fixed } kind = Rows;
+  size_t elem = 2;       // bytes per element
+  int64_t cols = 0;      // elements per row (Rows, Seqs)
+  size_t fixed_bytes = 0;
+  std::vector<unsigned char> init;
+};
+
+struct CompiledPlan {
+  bool f16 = true;
+  int length = 0, batch = 1, emb_size = 0;
+  std::vector<BufInfo> bufs;
+  std::map<std::string, int> buf_index;
+  std::vector<Step> steps;
+  std::string in_emb, in_mask, in_type;  // input buffer ids ("" when absent)
+  std::string out_buf;
+  int out_rows = 0, out_cols = 0;
+  bool out_per_seq = true;  // pooled head: one output row per sequence
+  int tile_q = 64;          // attention query tile of the launch list
+};
+
+// Device memory of one execution: plan buffers sized for `cap_rows` packed rows and
+// `cap_seqs` sequences, the sequence table and the f32 output.
+struct Exec {
+  Ctx* ctx = nullptr;
+  const CompiledPlan* cp = nullptr;
+  int64_t cap_rows = 0;
+  int cap_seqs = 0;
+  std::vector<void*> ptr;       // by buffer index (inputs may point into bulk storage)
+  std::vector<void*> owned;     // allocations to free
+  // current launch
+  int T = 0;                    // packed rows
+  SeqTable seq;                 // device pointers
+  int32_t* row_seq = nullptr;   // per packed row: sequence
+  // device sequence-table storage of this exec (plan mode)
+  int32_t* d_table = nullptr;
+  int64_t table_cap = 0;
+  float* d_out = nullptr;       // f32 output staging
+  int64_t out_cap = 0;
+  int64_t bytes = 0;
+  ~Exec();
+  void* buf(int i) const { return ptr[i]; }
+};
+
+void exec_alloc(Exec& ex, Ctx* ctx, const CompiledPlan* cp, int64_t cap_rows, int cap_seqs);
+void plan_compile(Ctx* ctx, const Json& plan, CompiledPlan& cp);
+void plan_check(Ctx* ctx, const Json& plan);
+// Builds the host sequence table: start, len, row_pos, row_seq, tiles for the given lengths.
+void build_seq_table(const std::vector<int32_t>& lens, int tile_q, std::vector<int32_t>& out, SeqTable& offsets,
+                     int64_t& total_rows);
+void exec_steps(Exec& ex, cudaStream_t st);
+void exec_output(Exec& ex, int rows_out, float* dst, cudaStream_t st);
+
+}  // namespace kh
