@@ -104,6 +104,12 @@ size_t kh_info(const kh_ctx* ctx, char* buf, size_t cap);
  * it covers), for profiles and tests. Same size convention as kh_info. */
 size_t kh_plan_launches(const kh_plan* plan, char* buf, size_t cap);
 
+/* Raw bytes of a plan buffer by id, written from / read into host memory: the CUDA counterpart
+ * of WasmPlan.view (src/plan/wasm.ts:473-476, "a plan buffer as f32 (tests, debugging)").
+ * Used by the per-op known-answer tests; a read waits for the context stream. */
+int kh_plan_buffer_write(kh_plan* plan, const char* id, const void* bytes, size_t len);
+int kh_plan_buffer_read(kh_plan* plan, const char* id, void* out, size_t len);
+
 /* Per-launch device times in ms of one forward over `rows` rows (CUDA events around every
  * launch), the CUDA counterpart of the WASM op profile (src/plan/wasm.ts:451-471) and of the
  * WebGPU dispatch profile (src/plan/executor.ts:303-361). Writes min(n, launches) values. */
@@ -142,7 +148,16 @@ int kh_run_batch(kh_bulk* bulk, const int32_t* seq_lens, int n, const void* emb,
  * number of kernel launches it made. */
 int kh_bulk_last_timing(const kh_bulk* bulk, float* ms, int64_t* launches);
 
+/* Per-step device times in ms of one bulk forward, summed over its chunks (CUDA events around
+ * every launch; one value per entry of kh_plan_launches). Not for timing runs: the events
+ * serialise the launches. */
+int kh_bulk_profile(kh_bulk* bulk, float* ms, size_t n);
+
 void kh_bulk_destroy(kh_bulk* bulk);
+
+/* The CUDA stream (cudaStream_t) every launch of this context goes to, so a caller can record
+ * its own events on it. The context owns the stream. */
+void* kh_ctx_stream(const kh_ctx* ctx);
 
 #ifdef __cplusplus
 }

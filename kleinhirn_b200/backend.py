@@ -46,6 +46,8 @@ _SIGS = {
     "kh_info": ([_P, ctypes.c_char_p, ctypes.c_size_t], ctypes.c_size_t),
     "kh_plan_launches": ([_P, ctypes.c_char_p, ctypes.c_size_t], ctypes.c_size_t),
     "kh_profile": ([_P, ctypes.c_int, _P, ctypes.c_size_t], ctypes.c_int),
+    "kh_plan_buffer_write": ([_P, ctypes.c_char_p, _P, ctypes.c_size_t], ctypes.c_int),
+    "kh_plan_buffer_read": ([_P, ctypes.c_char_p, _P, ctypes.c_size_t], ctypes.c_int),
     "kh_bulk_create": ([_P, ctypes.c_int64, ctypes.c_int, ctypes.c_int64, ctypes.POINTER(_P)], ctypes.c_int),
     "kh_bulk_set_lengths": ([_P, _P, ctypes.c_int], ctypes.c_int),
     "kh_bulk_upload": ([_P, _P, ctypes.c_size_t, _P, ctypes.c_size_t], ctypes.c_int),
@@ -55,6 +57,8 @@ _SIGS = {
                      ctypes.c_int),
     "kh_bulk_last_timing": ([_P, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_int64)], ctypes.c_int),
     "kh_bulk_destroy": ([_P], None),
+    "kh_bulk_profile": ([_P, _P, ctypes.c_size_t], ctypes.c_int),
+    "kh_ctx_stream": ([_P], ctypes.c_void_p),
 }
 
 _lib = None
@@ -155,6 +159,16 @@ class CudaPlanRunner:
         # The WASM backend throws the same way (src/wasm-backend.ts:90-96).
         raise NotImplementedError("the CUDA backend has no capture mode")
 
+    def write_buffer(self, bid: str, data: np.ndarray) -> None:
+        """Raw bytes into a plan buffer (WasmPlan.view for tests, src/plan/wasm.ts:473-476)."""
+        a = np.ascontiguousarray(data)
+        _check(self.lib, self.lib.kh_plan_buffer_write(self.handle, bid.encode(), _ptr(a), a.nbytes))
+
+    def read_buffer(self, bid: str, nbytes: int) -> np.ndarray:
+        out = np.empty(nbytes, dtype=np.uint8)
+        _check(self.lib, self.lib.kh_plan_buffer_read(self.handle, bid.encode(), _ptr(out), nbytes))
+        return out
+
     def launches(self) -> list[dict]:
         return json.loads(_string(self.lib.kh_plan_launches, self.handle))
 
@@ -214,6 +228,21 @@ class CudaBulk:
         self.upload(emb, type_ids)
         self.run()
         return self.read()
+
+    def profile(self) -> list[tuple[dict, float]]:
+        """Per-step device ms of one bulk forward (summed over chunks), with the launch list."""
+        steps = self.runner.launches()
+        ms = np.zeros(len(steps), dtype=np.float32)
+        _check(self.lib, self.lib.kh_bulk_profile(self.handle, _ptr(ms), ms.size))
+        return list(zip(steps, ms.tolist()))
+
+    def upload_ptr(self, emb_ptr: int, emb_bytes: int, type_ptr: int | None, type_len: int) -> None:
+        """Upload from raw host pointers (pinned buffers of the caller)."""
+        _check(self.lib, self.lib.kh_bulk_upload(self.handle, ctypes.c_void_p(emb_ptr), emb_bytes,
+                                                 None if type_ptr is None else ctypes.c_void_p(type_ptr), type_len))
+
+    def read_ptr(self, out_ptr: int, n: int) -> None:
+        _check(self.lib, self.lib.kh_bulk_read(self.handle, ctypes.c_void_p(out_ptr), n))
 
     def last_timing(self) -> tuple[float, int]:
         ms, n = ctypes.c_float(), ctypes.c_int64()
@@ -296,6 +325,11 @@ class CudaBackend:
 
     def info(self) -> dict:
         return json.loads(_string(self.lib.kh_info, self.handle))
+
+    @property
+    def stream(self) -> int:
+        """cudaStream_t of every launch of this backend (for caller-side CUDA events)."""
+        return int(self.lib.kh_ctx_stream(self.handle) or 0)
 
     def dispose(self) -> None:
         if self.handle:

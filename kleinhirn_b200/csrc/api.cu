@@ -217,7 +217,7 @@ int kh_plan_create(kh_ctx* ctx, const char* plan_json, size_t len, kh_plan** out
     }
     kh::plan_compile(c, plan, p->cp);
     const int64_t rows = int64_t(p->cp.length) * p->cp.batch;
-    kh::exec_alloc(p->ex, c, &p->cp, rows, p->cp.batch);
+    kh::exec_alloc(p->ex, c, &p->cp, rows, p->cp.batch, false);
   });
   if (st != KH_OK) return st;
   *out = p.release();
@@ -371,6 +371,33 @@ size_t kh_plan_launches(const kh_plan* plan, char* buf, size_t cap) {
   return put_string(o.str(), buf, cap);
 }
 
+int kh_plan_buffer_write(kh_plan* plan, const char* id, const void* bytes, size_t len) {
+  if (!plan || !id || (len && !bytes)) {
+    g_err = "kh_plan_buffer_write: null argument";
+    return KH_ERR_ARG;
+  }
+  Ctx* c = plan->owner->c.get();
+  return guard(c, Latch::Yes, [&] {
+    auto it = plan->cp.buf_index.find(id);
+    if (it == plan->cp.buf_index.end()) throw kh::ArgError(std::string("plan buffer ") + id + " has no memory");
+    KH_CUDA(cudaMemcpy(plan->ex.buf(it->second), bytes, len, cudaMemcpyHostToDevice));
+  });
+}
+
+int kh_plan_buffer_read(kh_plan* plan, const char* id, void* out, size_t len) {
+  if (!plan || !id || (len && !out)) {
+    g_err = "kh_plan_buffer_read: null argument";
+    return KH_ERR_ARG;
+  }
+  Ctx* c = plan->owner->c.get();
+  return guard(c, Latch::Yes, [&] {
+    auto it = plan->cp.buf_index.find(id);
+    if (it == plan->cp.buf_index.end()) throw kh::ArgError(std::string("plan buffer ") + id + " has no memory");
+    KH_CUDA(cudaStreamSynchronize(c->stream));
+    KH_CUDA(cudaMemcpy(out, plan->ex.buf(it->second), len, cudaMemcpyDeviceToHost));
+  });
+}
+
 int kh_profile(kh_plan* plan, int rows, float* ms, size_t n) {
   if (!plan || (n && !ms)) {
     g_err = "kh_profile: null argument";
@@ -416,7 +443,7 @@ int kh_bulk_create(kh_plan* plan, int64_t max_tokens, int max_seqs, int64_t chun
     b->max_seqs = max_seqs;
     b->chunk_tokens = chunk_tokens;
     const int cap_seqs = int(std::min<int64_t>(max_seqs, chunk_tokens));
-    kh::exec_alloc(b->ex, c, &cp, chunk_tokens, cap_seqs);
+    kh::exec_alloc(b->ex, c, &cp, chunk_tokens, cap_seqs, true);
     const size_t esz = cp.f16 ? 2 : 4;
     KH_CUDA(cudaMalloc(&b->d_emb, size_t(max_tokens) * cp.emb_size * esz + 256));
     if (!cp.in_type.empty()) KH_CUDA(cudaMalloc((void**)&b->d_type, size_t(max_tokens) * 4 + 256));
@@ -585,6 +612,53 @@ int kh_bulk_last_timing(const kh_bulk* bulk, float* ms, int64_t* launches) {
     if (launches) *launches = bulk->last_launches;
   });
 }
+
+int kh_bulk_profile(kh_bulk* bulk, float* ms, size_t n) {
+  if (!bulk || (n && !ms)) {
+    g_err = "kh_bulk_profile: null argument";
+    return KH_ERR_ARG;
+  }
+  Ctx* c = bulk->plan->owner->c.get();
+  return guard(c, Latch::Yes, [&] {
+    const kh::CompiledPlan& cp = bulk->plan->cp;
+    kh::Exec& ex = bulk->ex;
+    const size_t esz = cp.f16 ? 2 : 4;
+    const int ie = cp.buf_index.at(cp.in_emb), im = cp.buf_index.at(cp.in_mask);
+    const int it = cp.in_type.empty() ? -1 : cp.buf_index.at(cp.in_type);
+    const size_t ns = cp.steps.size() + 1;
+    std::vector<double> acc(ns, 0.0);
+    std::vector<cudaEvent_t> ev(ns + 1);
+    for (auto& e : ev) KH_CUDA(cudaEventCreate(&e));
+    for (const kh_bulk::Chunk& ch : bulk->chunks) {
+      ex.ptr[ie] = (char*)bulk->d_emb + size_t(ch.tok0) * cp.emb_size * esz;
+      ex.ptr[im] = bulk->d_mask + ch.tok0;
+      if (it >= 0) ex.ptr[it] = bulk->d_type + ch.tok0;
+      const int32_t* base = bulk->d_table + ch.word0;
+      ex.seq = rebase(ch.seq, base);
+      ex.row_seq = const_cast<int32_t*>(base) + (intptr_t)ch.seq.row_pos + ch.T;
+      ex.T = int(ch.T);
+      KH_CUDA(cudaEventRecord(ev[0], c->stream));
+      for (size_t i = 0; i < cp.steps.size(); ++i) {
+        cp.steps[i].run(ex, c->stream);
+        KH_CUDA(cudaEventRecord(ev[i + 1], c->stream));
+      }
+      float* dst = bulk->d_out + (cp.out_per_seq ? int64_t(ch.seq0) : ch.tok0) * cp.out_cols;
+      kh::exec_output(ex, cp.out_per_seq ? ch.S : int(ch.T), dst, c->stream);
+      KH_CUDA(cudaEventRecord(ev[ns], c->stream));
+      KH_CUDA(cudaGetLastError());
+      KH_CUDA(cudaEventSynchronize(ev[ns]));
+      for (size_t i = 0; i < ns; ++i) {
+        float t = 0;
+        KH_CUDA(cudaEventElapsedTime(&t, ev[i], ev[i + 1]));
+        acc[i] += t;
+      }
+    }
+    for (auto& e : ev) cudaEventDestroy(e);
+    for (size_t i = 0; i < ns && i < n; ++i) ms[i] = float(acc[i]);
+  });
+}
+
+void* kh_ctx_stream(const kh_ctx* ctx) { return ctx ? (void*)ctx->c->stream : nullptr; }
 
 void kh_bulk_destroy(kh_bulk* bulk) {
   if (!bulk) return;

@@ -146,6 +146,16 @@ __global__ void add_kernel(T* __restrict__ dst, const T* __restrict__ src, int64
 }
 
 template <typename T>
+__global__ void add_rows_kernel(T* __restrict__ dst, const T* __restrict__ src, int N, int rows,
+                                const int32_t* __restrict__ row_seq) {
+  const int64_t count = int64_t(rows) * N;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < count; i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = i / N;
+    st(dst, i, ld(dst, i) + ld(src, int64_t(row_seq[r]) * N + (i - r * N)));
+  }
+}
+
+template <typename T>
 __global__ void geglu_kernel(const T* __restrict__ mid, T* __restrict__ gate, int I, int rows) {
   const int64_t total = int64_t(rows) * I;
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
@@ -415,6 +425,13 @@ void launch_add(bool f16, void* dst, const void* src, int64_t count, cudaStream_
   if (count <= 0) return;
   if (f16) add_kernel<__half><<<grid_for(count, 256), 256, 0, st>>>((__half*)dst, (const __half*)src, count);
   else add_kernel<float><<<grid_for(count, 256), 256, 0, st>>>((float*)dst, (const float*)src, count);
+}
+
+void launch_add_rows(bool f16, void* dst, const void* src, int N, int rows, const int32_t* row_seq, cudaStream_t st) {
+  const int64_t count = int64_t(rows) * N;
+  if (count <= 0) return;
+  if (f16) add_rows_kernel<__half><<<grid_for(count, 256), 256, 0, st>>>((__half*)dst, (const __half*)src, N, rows, row_seq);
+  else add_rows_kernel<float><<<grid_for(count, 256), 256, 0, st>>>((float*)dst, (const float*)src, N, rows, row_seq);
 }
 
 void launch_geglu(bool f16, const void* mid, void* gate, int I, int rows, cudaStream_t st) {

@@ -35,6 +35,9 @@ void launch_layernorm(bool f16, const void* a, const void* b, const void* w, con
 // add.wgsl MODE 0: dst += src over count elements (storage rounding).
 void launch_add(bool f16, void* dst, const void* src, int64_t count, cudaStream_t st);
 
+// add.wgsl MODE 1: dst[r, :] += src[sequence of r, :] (one source row per sequence).
+void launch_add_rows(bool f16, void* dst, const void* src, int N, int rows, const int32_t* row_seq, cudaStream_t st);
+
 // geglu.wgsl: gate[r, j] = gelu(mid[r, j]) * mid[r, I + j].
 void launch_geglu(bool f16, const void* mid, void* gate, int I, int rows, cudaStream_t st);
 

@@ -181,7 +181,6 @@ void plan_check(Ctx* ctx, const Json& plan) {
       bool ok = false;
       for (const char* s : SUPPORTED) ok = ok || k == s;
       if (!ok) throw PlanError("plan op " + op["name"].as_str() + ": kernel " + k + " has no CUDA computation");
-      if (k == "add" && cint(op, "MODE") != 0) throw PlanError("add MODE 1 (Julia type rows) is not planned here");
       if ((k == "layernorm" || k == "embln") && cint(op, "N") > 1024)
         throw PlanError("plan op " + op["name"].as_str() + ": norm width above 1024");
       if ((k == "attention" || k == "mbattention" || k == "mbflash" || k == "attscore") && cint(op, "D") > 64)
@@ -227,6 +226,7 @@ void plan_compile(Ctx* ctx, const Json& plan, CompiledPlan& cp) {
     auto dit = decl.find(id);
     if (dit == decl.end()) throw PlanError("plan: buffer " + id + " is not declared");
     const Json& d = *dit->second;
+    b.decl_bytes = size_t(d["bytes"].as_int());
     if (d.has("init_b64")) {
       b.kind = BufInfo::Fixed;
       b.init = base64_decode(d["init_b64"].as_str());
@@ -345,6 +345,7 @@ void plan_compile(Ctx* ctx, const Json& plan, CompiledPlan& cp) {
     const bool fixed_rows = seq_level(op);
     if (is_matmul(k)) {
       const int N = cint(op, "N"), K = cint(op, "K"), act = cint(op, "ACT");
+      const int fixed_m = cint(op, "M");
       const std::string a_id = bind(op, 0), c_id = bind(op, 3);
       const void* W = wptr(bind(op, 1));
       Ref bias = ref(bind(op, 2));
@@ -396,7 +397,7 @@ void plan_compile(Ctx* ctx, const Json& plan, CompiledPlan& cp) {
         const bool bias_zero = !bias.weight;
         Step s;
         s.run = [=](Exec& ex, cudaStream_t st) {
-          const int M = fixed_rows ? ex.seq.count : ex.T;
+          const int M = fixed_rows ? (ex.bulk ? ex.seq.count : fixed_m) : ex.T;
           const void* bp = bias_zero ? nullptr : fb(ex);
           GemmEpilogue e = epi;
           if (itab >= 0) { e.table = (const float*)ex.buf(itab); e.row_pos = ex.seq.row_pos; }
@@ -409,6 +410,7 @@ void plan_compile(Ctx* ctx, const Json& plan, CompiledPlan& cp) {
     }
     if (k == "layernorm") {
       const int N = cint(op, "N"), mode = cint(op, "MODE");
+      const int fixed_n = fixed_rows ? int(op["dispatch"][0].as_int()) : 0;
       const float eps = float(cnum(op, "EPS"));
       const std::string a = bind(op, 0), b2 = bind(op, 1), m = bind(op, 4), o = bind(op, 5);
       Ref w = ref(bind(op, 2)), bb = ref(bind(op, 3));
@@ -418,7 +420,7 @@ void plan_compile(Ctx* ctx, const Json& plan, CompiledPlan& cp) {
         auto fbb = resolve(c, bb);
         Step s;
         s.run = [=](Exec& ex, cudaStream_t st) {
-          const int rows = fixed_rows ? ex.seq.count : ex.T;
+          const int rows = fixed_rows ? (ex.bulk ? ex.seq.count : fixed_n) : ex.T;
           launch_layernorm(f16, ex.buf(ia), ex.buf(ib), fw(ex), fbb(ex), (const float*)ex.buf(im), ex.buf(io), N,
                            rows, mode, eps, st);
         };
@@ -446,12 +448,15 @@ void plan_compile(Ctx* ctx, const Json& plan, CompiledPlan& cp) {
       continue;
     }
     if (k == "add") {
-      const int N = cint(op, "N");
+      const int N = cint(op, "N"), mode = cint(op, "MODE");
       const std::string d = bind(op, 0), sname = bind(op, 1);
       protos.push_back({"add", {name}, [=](const CompiledPlan& c) {
         const int id = bi(c, d), is = bi(c, sname);
         Step s;
-        s.run = [=](Exec& ex, cudaStream_t st) { launch_add(f16, ex.buf(id), ex.buf(is), int64_t(ex.T) * N, st); };
+        s.run = [=](Exec& ex, cudaStream_t st) {
+          if (mode == 0) launch_add(f16, ex.buf(id), ex.buf(is), int64_t(ex.T) * N, st);
+          else launch_add_rows(f16, ex.buf(id), ex.buf(is), N, ex.T, ex.row_seq, st);
+        };
         return s;
       }});
       continue;
@@ -549,8 +554,9 @@ void plan_compile(Ctx* ctx, const Json& plan, CompiledPlan& cp) {
   }
 }
 
-void exec_alloc(Exec& ex, Ctx* ctx, const CompiledPlan* cp, int64_t cap_rows, int cap_seqs) {
+void exec_alloc(Exec& ex, Ctx* ctx, const CompiledPlan* cp, int64_t cap_rows, int cap_seqs, bool bulk) {
   ex.ctx = ctx;
+  ex.bulk = bulk;
   ex.cp = cp;
   ex.cap_rows = cap_rows;
   ex.cap_seqs = cap_seqs;
@@ -561,6 +567,7 @@ void exec_alloc(Exec& ex, Ctx* ctx, const CompiledPlan* cp, int64_t cap_rows, in
     if (b.kind == BufInfo::Fixed) bytes = std::max(b.fixed_bytes, b.init.size());
     else if (b.kind == BufInfo::Rows) bytes = size_t(cap_rows) * size_t(b.cols) * b.elem;
     else bytes = size_t(cap_seqs) * size_t(b.cols) * b.elem;
+    if (!bulk) bytes = std::max(bytes, b.decl_bytes);
     bytes = (bytes + 255) / 256 * 256 + 256;
     void* p = nullptr;
     KH_CUDA(cudaMalloc(&p, bytes));
@@ -570,7 +577,7 @@ void exec_alloc(Exec& ex, Ctx* ctx, const CompiledPlan* cp, int64_t cap_rows, in
     ex.ptr[i] = p;
     ex.bytes += int64_t(bytes);
   }
-  const int64_t out_rows = cp->out_per_seq ? cap_seqs : cap_rows;
+  const int64_t out_rows = std::max<int64_t>(cp->out_per_seq ? cap_seqs : cap_rows, bulk ? 0 : cp->out_rows);
   ex.out_cap = out_rows * cp->out_cols;
   KH_CUDA(cudaMalloc((void**)&ex.d_out, size_t(ex.out_cap) * 4 + 256));
   ex.owned.push_back(ex.d_out);

@@ -74,6 +74,7 @@ struct BufInfo {
   size_t elem = 2;       // bytes per element
   int64_t cols = 0;      // elements per row (Rows, Seqs)
   size_t fixed_bytes = 0;
+  size_t decl_bytes = 0;  // the plan's declared size (plan-mode executions allocate at least this)
   std::vector<unsigned char> init;
 };
 
@@ -99,6 +100,7 @@ struct Exec {
   int cap_seqs = 0;
   std::vector<void*> ptr;       // by buffer index (inputs may point into bulk storage)
   std::vector<void*> owned;     // allocations to free
+  bool bulk = false;            // ragged bulk execution (fixed-dispatch ops run once per sequence)
   // current launch
   int T = 0;                    // packed rows
   SeqTable seq;                 // device pointers
@@ -113,7 +115,7 @@ struct Exec {
   void* buf(int i) const { return ptr[i]; }
 };
 
-void exec_alloc(Exec& ex, Ctx* ctx, const CompiledPlan* cp, int64_t cap_rows, int cap_seqs);
+void exec_alloc(Exec& ex, Ctx* ctx, const CompiledPlan* cp, int64_t cap_rows, int cap_seqs, bool bulk);
 void plan_compile(Ctx* ctx, const Json& plan, CompiledPlan& cp);
 void plan_check(Ctx* ctx, const Json& plan);
 // Builds the host sequence table: start, len, row_pos, row_seq, tiles for the given lengths.

@@ -1,0 +1,113 @@
+"""Model-level parity of the CUDA backend with the oracle, through the C ABI.
+
+Acceptance rules: f32 plans give identical argmax and cosine >= 0.9999
+against the oracle; f16 plans give cosine >= 0.999 and outputs within 2e-2 absolute (scaled by
+max(1, |output|)) against the oracle run in f32 on the same f16 weights. Ragged bulk runs give
+the B = 1 results of every sequence."""
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from harness import Model, cosine_rows, cuda_forward_bulk, cuda_forward_plan, oracle_forward
+from kleinhirn_b200 import synthetic
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = json.loads((Path(__file__).parent / "golden" / "forward_golden.json").read_text())
+F16_ABS = 2e-2
+
+
+@pytest.fixture(scope="module")
+def backend_factory():
+    from kleinhirn_b200.backend import CudaBackend
+    made = []
+
+    def make(m):
+        be = CudaBackend(m.weights)
+        made.append(be)
+        return be
+    yield make
+    for b in made:
+        b.dispose()
+
+
+def assert_f32(got, want):
+    cos = cosine_rows(got, want)
+    assert cos.min() >= 0.9999, cos
+    if want.shape[1] > 1:
+        assert np.array_equal(np.argmax(got, 1), np.argmax(want, 1))
+
+
+def assert_f16(got, want):
+    cos = cosine_rows(got, want)
+    assert cos.min() >= 0.999, cos
+    scale = max(1.0, float(np.abs(want).max()))
+    assert np.abs(got - want).max() <= F16_ABS * scale, np.abs(got - want).max()
+
+
+@pytest.mark.parametrize("case", GOLDEN["cases"], ids=[c["name"] for c in GOLDEN["cases"]])
+@pytest.mark.parametrize("f16", [False, True], ids=["f32", "f16"])
+def test_family_parity_plan_and_bulk(case, f16, backend_factory):
+    m = Model(case["config"], case["extras"], seed=case["seed"], f16=f16)
+    be = backend_factory(m)
+    ids = [it["ids"] for it in case["items"]]
+    want = oracle_forward(m, ids, 32)
+    got = cuda_forward_plan(be, m, ids, 32)
+    (assert_f16 if f16 else assert_f32)(got, want)
+    if not f16:
+        # the reference's own float64 forward, through the golden file
+        ref = np.array([it["want"] for it in case["items"]])
+        assert cosine_rows(got, ref).min() >= 0.9999
+    bulk = cuda_forward_bulk(be, m, ids, 32, chunk_tokens=48)
+    assert np.allclose(bulk, got, rtol=1e-5, atol=1e-5), np.abs(bulk - got).max()
+
+
+def baseline_case(name, layers, lengths, bucket, seed=7):
+    cfg = dict(synthetic.CONFIGS[name]["config"])
+    if name == "distilbert":
+        cfg["n_layers"] = layers
+    else:
+        cfg["num_hidden_layers"] = layers
+    cfg["vocab_size"] = 512
+    if name == "deberta-v3-base":
+        pass
+    m = Model(cfg, synthetic.CONFIGS[name]["extras"], seed=seed, f16=synthetic.CONFIGS[name]["f16"])
+    c = synthetic.CONFIGS[name]
+    ids = synthetic.token_ids(name, lengths, seed)
+    ids = [np.minimum(x, 511) for x in ids]
+    return m, ids
+
+
+@pytest.mark.parametrize("name,layers,lengths,bucket", [
+    ("minilm-l6", 2, [128, 77], 128),
+    ("roberta-base", 2, [128, 40], 128),
+    ("deberta-v3-base", 1, [512, 300], 512),
+    ("modernbert-base", 3, [45, 200, 8, 512], 512),
+    ("mminilm-l12-xlmr", 2, [142, 36, 300], 512),
+])
+def test_baseline_configs_full_width(name, layers, lengths, bucket, backend_factory):
+    m, ids = baseline_case(name, layers, lengths, bucket)
+    be = backend_factory(m)
+    want = oracle_forward(m, ids, bucket, threads=8)
+    got = cuda_forward_plan(be, m, ids, bucket)
+    (assert_f16 if m.f16 else assert_f32)(got, want)
+    bulk = cuda_forward_bulk(be, m, ids, bucket, chunk_tokens=max(bucket, 600))
+    assert np.allclose(bulk, got, rtol=1e-4, atol=1e-4), np.abs(bulk - got).max()
+
+
+def test_batch_plan_matches_single_calls(backend_factory):
+    """A batch plan (B = 4 at a 64-row stride, src/encoder.ts:407-448) gives each row's B = 1 output."""
+    from kleinhirn_b200.encoder import Encoder
+    case = GOLDEN["cases"][1]
+    m = Model(case["config"], case["extras"], seed=case["seed"], f16=True)
+    be = backend_factory(m)
+    enc = Encoder(be, m.spec, m.head, m.word_table, buckets=(32, 64), f16=True)
+    rng = np.random.default_rng(3)
+    id_lists = [list(rng.integers(3, 96, n)) for n in (5, 17, 31, 9, 60, 2)]
+    single = np.stack([enc.run_ids(x) for x in id_lists])
+    batched = np.stack(enc.run_ids_batch(id_lists))
+    ragged = enc.run_ragged(id_lists)
+    assert np.allclose(batched, single, atol=1e-3), np.abs(batched - single).max()
+    assert np.allclose(ragged, single, atol=1e-5), np.abs(ragged - single).max()
