@@ -9,6 +9,8 @@
 #include <vector>
 
 #include "../../include/kh_cuda.h"
+#include "attn_tc.h"
+#include "gemm_tc.h"
 #include "runtime.h"
 
 using kh::Ctx;
@@ -98,6 +100,16 @@ kh::SeqTable rebase(const kh::SeqTable& o, const int32_t* base) {
   s.row_pos = base + (intptr_t)o.row_pos;
   s.tiles = base + (intptr_t)o.tiles;
   return s;
+}
+
+// A tensor-core pipeline wait that gave up leaves a code on the device; after a sync it becomes
+// a CUDA error of the call (and latches like one).
+void check_pipelines() {
+  const int g = kh::tc_error_code();
+  const int a = kh::attn_error_code();
+  if (g || a)
+    throw kh::CudaError("tensor-core pipeline wait timed out (gemm code " + std::to_string(g) + ", attention code " +
+                        std::to_string(a) + ")");
 }
 
 std::string json_escape(const std::string& s) {
@@ -320,6 +332,7 @@ int kh_read_output(kh_plan* plan, float* out, size_t n) {
                                      std::to_string(need));
     KH_CUDA(cudaMemcpyAsync(out, plan->ex.d_out, need * 4, cudaMemcpyDeviceToHost, c->stream));
     KH_CUDA(cudaStreamSynchronize(c->stream));
+    check_pipelines();
   });
 }
 
@@ -588,6 +601,7 @@ int kh_bulk_read(kh_bulk* bulk, float* out, size_t n) {
                                      std::to_string(need));
     KH_CUDA(cudaMemcpyAsync(out, bulk->d_out, need * 4, cudaMemcpyDeviceToHost, c->stream));
     KH_CUDA(cudaStreamSynchronize(c->stream));
+    check_pipelines();
   });
 }
 

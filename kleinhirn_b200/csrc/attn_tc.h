@@ -11,4 +11,7 @@ int attention_tile_q(bool f16);
 
 void launch_attention(bool f16, const AttnArgs& a, const SeqTable& seq, cudaStream_t st);
 
+// Code of the first tensor-core attention wait that gave up (0: none); read after a sync.
+int attn_error_code();
+
 }  // namespace kh

@@ -34,3 +34,8 @@ void launch_gemm(Ctx* ctx, bool f16, const void* A, const void* W, const void* b
                  int act, const GemmEpilogue& e, cudaStream_t st);
 
 }  // namespace kh
+
+namespace kh {
+// Code of the first tensor-core pipeline wait that gave up (0: none); read after a sync.
+int tc_error_code();
+}  // namespace kh
