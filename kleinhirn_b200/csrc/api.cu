@@ -98,7 +98,9 @@ kh::SeqTable rebase(const kh::SeqTable& o, const int32_t* base) {
   s.start = base + (intptr_t)o.start;
   s.len = base + (intptr_t)o.len;
   s.row_pos = base + (intptr_t)o.row_pos;
+  s.row_seq = base + (intptr_t)o.row_seq;
   s.tiles = base + (intptr_t)o.tiles;
+  s.ptiles = base + (intptr_t)o.ptiles;
   return s;
 }
 

@@ -28,6 +28,7 @@
 
 #include "gemm_tc.h"
 #include "sm100.cuh"
+#include "tmap.h"
 
 namespace kh {
 
@@ -315,58 +316,6 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
-// ---- host side ----
-
-typedef CUresult (*EncodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiled encode_fn() {
-  static EncodeTiled fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiled>(p);
-  });
-  if (!fn) throw CudaError("cuTensorMapEncodeTiled is unavailable");
-  return fn;
-}
-
-// Tensor map of a row-major f16 matrix [rows, cols] with boxes of 64 columns x box_rows rows,
-// 128-byte swizzle, zero fill outside. Cached by (pointer, shape, box).
-const CUtensorMap& tensor_map(const void* ptr, uint64_t rows, uint64_t cols, uint32_t box_rows) {
-  static std::mutex mu;
-  static std::map<std::tuple<const void*, uint64_t, uint64_t, uint32_t>, CUtensorMap> cache;
-  std::lock_guard<std::mutex> lk(mu);
-  auto key = std::make_tuple(ptr, rows, cols, box_rows);
-  auto it = cache.find(key);
-  if (it != cache.end()) return it->second;
-  if (cache.size() > 8192) cache.clear();
-  CUtensorMap m;
-  const cuuint64_t dims[2] = {cols, rows};
-  const cuuint64_t strides[1] = {cols * 2};
-  const cuuint32_t box[2] = {BK, box_rows};
-  const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
-                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) throw CudaError("cuTensorMapEncodeTiled failed: " + std::to_string(int(r)));
-  return cache.emplace(key, m).first->second;
-}
-
-int num_sms() {
-  static int sms = 0;
-  if (!sms) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  }
-  return sms;
-}
-
 }  // namespace
 
 bool gemm_tc_supported(int N, int K) { return N >= 32 && N % 32 == 0 && K % 8 == 0 && K >= 16; }
@@ -455,10 +404,11 @@ void launch_gemm(Ctx* ctx, bool f16, const void* A, const void* W, const void* b
     p.D = e.D;
     p.rope_cols = 2 * e.H * e.D;
   }
-  const CUtensorMap& ma = tensor_map(A, uint64_t(M), uint64_t(K), BM);
-  const CUtensorMap& mb = tensor_map(W, uint64_t(N), uint64_t(K), BN);
+  const CUtensorMap& ma = tensor_map_f16(A, uint64_t(M), uint64_t(K), uint64_t(K), BK, BM, 128);
+  const CUtensorMap& mb = tensor_map_f16(W, uint64_t(N), uint64_t(K), uint64_t(K), BK, BN, 128);
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-  const int grid = std::min(tiles, num_sms());
+  static const int sms = device_sms();
+  const int grid = std::min(tiles, sms);
   gemm_tc_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(ma, mb, p);
 }
 

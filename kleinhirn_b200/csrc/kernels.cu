@@ -139,6 +139,137 @@ __global__ void layernorm_kernel(const T* __restrict__ a, const T* __restrict__ 
   }
 }
 
+// Vectorised forms of the two row kernels: 16-byte loads and stores (8 f16 or 4 f32 per lane
+// and step), one warp per row, the row in registers between the passes. N % (16 / sizeof(T)) == 0.
+template <typename T> struct Vec;
+template <> struct Vec<__half> {
+  static constexpr int N = 8;
+  __device__ static void load(const __half* p, float* out) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __half22float2(h[e]);
+      out[2 * e] = f.x;
+      out[2 * e + 1] = f.y;
+    }
+  }
+  __device__ static void store(__half* p, const float* v) {
+    __half2 h[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) h[e] = __floats2half2_rn(v[2 * e], v[2 * e + 1]);
+    *reinterpret_cast<uint4*>(p) = *reinterpret_cast<uint4*>(h);
+  }
+};
+template <> struct Vec<float> {
+  static constexpr int N = 4;
+  __device__ static void load(const float* p, float* out) {
+    const float4 f = *reinterpret_cast<const float4*>(p);
+    out[0] = f.x; out[1] = f.y; out[2] = f.z; out[3] = f.w;
+  }
+  __device__ static void store(float* p, const float* v) {
+    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  }
+};
+
+constexpr int MAXV = 4;  // vectors per lane: N <= 32 * 4 * 8 (f16) or 32 * 4 * 4 (f32)
+
+// x: the row as nv vectors of Vec<T>::N values, v[k] holds vector lane + 32 k.
+template <typename T>
+__device__ __forceinline__ void ln_vec_finish(float (&v)[MAXV][8], int N, const T* __restrict__ w,
+                                              const T* __restrict__ bias, float eps, float scale, T* __restrict__ out) {
+  constexpr int VN = Vec<T>::N;
+  const int lane = threadIdx.x & 31;
+  const int nv = N / VN;
+  float s = 0.f;
+#pragma unroll
+  for (int k = 0; k < MAXV; ++k)
+    if (lane + 32 * k < nv)
+#pragma unroll
+      for (int e = 0; e < VN; ++e) s += v[k][e];
+  const float mean = warp_sum(s) / float(N);
+  float q = 0.f;
+#pragma unroll
+  for (int k = 0; k < MAXV; ++k)
+    if (lane + 32 * k < nv)
+#pragma unroll
+      for (int e = 0; e < VN; ++e) {
+        const float x = v[k][e] - mean;
+        q += x * x;
+      }
+  const float inv = 1.0f / sqrtf(warp_sum(q) / float(N) + eps);
+#pragma unroll
+  for (int k = 0; k < MAXV; ++k) {
+    const int idx = lane + 32 * k;
+    if (idx < nv) {
+      float wv[8], bv[8], y[8];
+      Vec<T>::load(w + idx * VN, wv);
+      Vec<T>::load(bias + idx * VN, bv);
+#pragma unroll
+      for (int e = 0; e < VN; ++e) y[e] = ((v[k][e] - mean) * inv * wv[e] + bv[e]) * scale;
+      Vec<T>::store(out + idx * VN, y);
+    }
+  }
+}
+
+template <typename T>
+__global__ void layernorm_vec_kernel(const T* __restrict__ a, const T* __restrict__ bb, const T* __restrict__ w,
+                                     const T* __restrict__ bias, const float* __restrict__ mask, T* __restrict__ out,
+                                     int N, int rows, int mode, float eps) {
+  constexpr int VN = Vec<T>::N;
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int lane = threadIdx.x & 31;
+  const int nv = N / VN;
+  const int64_t base = int64_t(row) * N;
+  float v[MAXV][8];
+#pragma unroll
+  for (int k = 0; k < MAXV; ++k) {
+    const int idx = lane + 32 * k;
+    if (idx < nv) {
+      Vec<T>::load(a + base + idx * VN, v[k]);
+      if (mode == 2) {
+        float y[8];
+        Vec<T>::load(bb + base + idx * VN, y);
+#pragma unroll
+        for (int e = 0; e < VN; ++e) v[k][e] += y[e];
+      }
+    }
+  }
+  ln_vec_finish<T>(v, N, w, bias, eps, mode == 1 ? mask[row] : 1.0f, out + base);
+}
+
+template <typename T>
+__global__ void embln_vec_kernel(const T* __restrict__ word, const T* __restrict__ pos, const T* __restrict__ typ,
+                                 const uint32_t* __restrict__ tt, const T* __restrict__ w, const T* __restrict__ b,
+                                 const float* __restrict__ mask, T* __restrict__ out, int N, int rows,
+                                 const int32_t* __restrict__ row_pos, int offset, int maxpos, float eps, int maskmul,
+                                 int posids) {
+  constexpr int VN = Vec<T>::N;
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int lane = threadIdx.x & 31;
+  const uint32_t t = tt ? tt[row] : 0u;
+  int prow = posids ? int(t >> 16) : row_pos[row] + offset;
+  prow = min(prow, maxpos - 1);
+  const int64_t wbase = int64_t(row) * N, pbase = int64_t(prow) * N, tbase = int64_t(t & 0xffffu) * N;
+  const int nv = N / VN;
+  float v[MAXV][8];
+#pragma unroll
+  for (int k = 0; k < MAXV; ++k) {
+    const int idx = lane + 32 * k;
+    if (idx < nv) {
+      float x[8], y[8], z[8];
+      Vec<T>::load(word + wbase + idx * VN, x);
+      Vec<T>::load(pos + pbase + idx * VN, y);
+      Vec<T>::load(typ + tbase + idx * VN, z);
+#pragma unroll
+      for (int e = 0; e < VN; ++e) v[k][e] = x[e] + y[e] + z[e];
+    }
+  }
+  ln_vec_finish<T>(v, N, w, b, eps, maskmul ? mask[row] : 1.0f, out + wbase);
+}
+
 template <typename T>
 __global__ void add_kernel(T* __restrict__ dst, const T* __restrict__ src, int64_t count) {
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < count; i += int64_t(gridDim.x) * blockDim.x)
@@ -397,6 +528,19 @@ void launch_embln(bool f16, const void* word, const void* pos, const void* typ, 
                   int maxpos, float eps, int maskmul, int posids, cudaStream_t st) {
   if (N > 32 * MAXE) throw std::runtime_error("embln: width above 1024");
   if (rows <= 0) return;
+  const int vn = f16 ? 8 : 4;
+  if (N % vn == 0 && N / vn <= 32 * MAXV) {
+    const int g4 = (rows + 3) / 4;
+    if (f16)
+      embln_vec_kernel<__half><<<g4, 128, 0, st>>>((const __half*)word, (const __half*)pos, (const __half*)typ, tt,
+                                                   (const __half*)w, (const __half*)b, mask, (__half*)out, N, rows,
+                                                   row_pos, offset, maxpos, eps, maskmul, posids);
+    else
+      embln_vec_kernel<float><<<g4, 128, 0, st>>>((const float*)word, (const float*)pos, (const float*)typ, tt,
+                                                  (const float*)w, (const float*)b, mask, (float*)out, N, rows,
+                                                  row_pos, offset, maxpos, eps, maskmul, posids);
+    return;
+  }
   const int grid = (rows + 7) / 8;
   if (f16)
     embln_kernel<__half><<<grid, 256, 0, st>>>((const __half*)word, (const __half*)pos, (const __half*)typ, tt,
@@ -412,6 +556,17 @@ void launch_layernorm(bool f16, const void* a, const void* b, const void* w, con
                       void* out, int N, int rows, int mode, float eps, cudaStream_t st) {
   if (N > 32 * MAXE) throw std::runtime_error("layernorm: width above 1024");
   if (rows <= 0) return;
+  const int vn = f16 ? 8 : 4;
+  if (N % vn == 0 && N / vn <= 32 * MAXV) {
+    const int g4 = (rows + 3) / 4;
+    if (f16)
+      layernorm_vec_kernel<__half><<<g4, 128, 0, st>>>((const __half*)a, (const __half*)b, (const __half*)w,
+                                                       (const __half*)bias, mask, (__half*)out, N, rows, mode, eps);
+    else
+      layernorm_vec_kernel<float><<<g4, 128, 0, st>>>((const float*)a, (const float*)b, (const float*)w,
+                                                      (const float*)bias, mask, (float*)out, N, rows, mode, eps);
+    return;
+  }
   const int grid = (rows + 7) / 8;
   if (f16)
     layernorm_kernel<__half><<<grid, 256, 0, st>>>((const __half*)a, (const __half*)b, (const __half*)w,

@@ -20,7 +20,14 @@ struct SeqTable {
   int max_len = 0;   // longest sequence
   const int32_t* tiles = nullptr;  // attention work tiles: (seq, q0) pairs
   int ntiles = 0;
+  const int32_t* row_seq = nullptr;  // sequence of every packed row
+  // Packed attention tiles of the tensor-core kernel: 128 consecutive packed rows (q0) and the
+  // packed key rows [kstart, kend) of every sequence those rows belong to.
+  const int32_t* ptiles = nullptr;   // (q0, kstart, kend) triples
+  int nptiles = 0;
 };
+
+constexpr int PACKED_TILE = 128;
 
 // embln.wgsl / src/wasm/plan.ts:434-447: word + position + type, two-pass LN, optional x mask.
 void launch_embln(bool f16, const void* word, const void* pos, const void* typ, const uint32_t* tt,
@@ -76,6 +83,7 @@ struct AttnArgs {
   const void* pos_query = nullptr;
   const uint32_t* relidx = nullptr;
   int L = 0;           // bucket length: relidx is L x L
+  int rows = 0;        // packed rows of the launch
 };
 void launch_attention_simt(bool f16, const AttnArgs& a, const SeqTable& seq, cudaStream_t st);
 

@@ -330,6 +330,7 @@ void plan_compile(Ctx* ctx, const Json& plan, CompiledPlan& cp) {
           a.H = g.H; a.D = g.D; a.scale = g.scale; a.window = g.window; a.rel = g.rel;
           a.pos_key = pk; a.pos_query = pq; a.relidx = ir >= 0 ? (const uint32_t*)ex.buf(ir) : nullptr;
           a.L = g.L;
+          a.rows = ex.T;
           launch_attention(f16, a, ex.seq, st);
         };
         return s;
@@ -503,9 +504,17 @@ void plan_compile(Ctx* ctx, const Json& plan, CompiledPlan& cp) {
       const std::string mk = bind(op, 0), x = bind(op, 1), o = bind(op, 2);
       protos.push_back({"gather", {name}, [=](const CompiledPlan& c) {
         const int imk = bi(c, mk), ix = bi(c, x), io = bi(c, o);
+        // The pooled heads bind an all-zero marker buffer sized for the plan's batch ('first',
+        // src/plan/build.ts:304-310,482): marker 0 of every sequence, the CLS row. It is not read,
+        // so a launch with more sequences than the plan's batch (bulk runs) stays in bounds.
+        const BufInfo& mb = c.bufs[imk];
+        const bool zero_markers =
+            !mb.init.empty() && std::all_of(mb.init.begin(), mb.init.end(), [](unsigned char v) { return v == 0; });
         Step s;
         s.run = [=](Exec& ex, cudaStream_t st) {
-          launch_gather(f16, ex.buf(ix), ex.buf(io), D, ex.seq, (const uint32_t*)ex.buf(imk), K, st);
+          if (!zero_markers && ex.bulk) throw PlanError("gather with marker indices has no bulk form");
+          launch_gather(f16, ex.buf(ix), ex.buf(io), D, ex.seq,
+                        zero_markers ? nullptr : (const uint32_t*)ex.buf(imk), K, st);
         };
         return s;
       }});
@@ -596,12 +605,14 @@ void build_seq_table(const std::vector<int32_t>& lens, int tile_q, std::vector<i
     ntiles += (l + tile_q - 1) / tile_q;
     max_len = std::max(max_len, int(l));
   }
-  out.assign(size_t(2 * S + 2 * T + 2 * ntiles), 0);
+  const int nptiles = int((T + PACKED_TILE - 1) / PACKED_TILE);
+  out.assign(size_t(2 * S + 2 * T + 2 * ntiles + 3 * nptiles), 0);
   int32_t* start = out.data();
   int32_t* len = start + S;
   int32_t* pos = len + S;
   int32_t* rseq = pos + T;
   int32_t* tiles = rseq + T;
+  int32_t* ptiles = tiles + 2 * ntiles;
   int64_t r = 0;
   int t = 0;
   for (int s = 0; s < S; ++s) {
@@ -618,14 +629,26 @@ void build_seq_table(const std::vector<int32_t>& lens, int tile_q, std::vector<i
     }
     r += lens[s];
   }
+  // packed tiles: keys of every sequence the tile's 128 rows belong to
+  for (int p = 0; p < nptiles; ++p) {
+    const int64_t q0 = int64_t(p) * PACKED_TILE;
+    const int64_t q1 = std::min<int64_t>(q0 + PACKED_TILE, T) - 1;
+    const int s0 = rseq[q0], s1 = rseq[q1];
+    ptiles[3 * p] = int32_t(q0);
+    ptiles[3 * p + 1] = start[s0];
+    ptiles[3 * p + 2] = start[s1] + len[s1];
+  }
   // offsets (in words) stored in the pointer fields, rebased by the caller
   offs.start = (const int32_t*)(intptr_t)0;
   offs.len = (const int32_t*)(intptr_t)S;
   offs.row_pos = (const int32_t*)(intptr_t)(2 * S);
+  offs.row_seq = (const int32_t*)(intptr_t)(2 * S + T);
   offs.tiles = (const int32_t*)(intptr_t)(2 * S + 2 * T);
+  offs.ptiles = (const int32_t*)(intptr_t)(2 * S + 2 * T + 2 * ntiles);
   offs.count = S;
   offs.max_len = max_len;
   offs.ntiles = ntiles;
+  offs.nptiles = nptiles;
   total_rows = T;
 }
 

@@ -1,0 +1,69 @@
+// TMA tensor-map encoding through the driver entry point, cached per (pointer, geometry).
+
+#include <map>
+#include <mutex>
+#include <string>
+#include <tuple>
+
+#include "runtime.h"
+#include "tmap.h"
+
+namespace kh {
+
+namespace {
+
+typedef CUresult (*EncodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+  static EncodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiled>(p);
+  });
+  if (!fn) throw CudaError("cuTensorMapEncodeTiled is unavailable");
+  return fn;
+}
+
+}  // namespace
+
+const CUtensorMap& tensor_map_f16(const void* ptr, uint64_t rows, uint64_t cols, uint64_t row_stride,
+                                  uint32_t box_cols, uint32_t box_rows, int swizzle_bytes) {
+  static std::mutex mu;
+  static std::map<std::tuple<const void*, uint64_t, uint64_t, uint64_t, uint32_t, uint32_t, int>, CUtensorMap> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  const auto key = std::make_tuple(ptr, rows, cols, row_stride, box_cols, box_rows, swizzle_bytes);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  if (cache.size() > 8192) cache.clear();
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (row_stride * 2) % 16)
+    throw PlanError("tensor map: base or row stride not 16-byte aligned");
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {row_stride * 2};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapSwizzle sw = swizzle_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                : swizzle_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                                      : CU_TENSOR_MAP_SWIZZLE_NONE;
+  const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
+                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw CudaError("cuTensorMapEncodeTiled failed: " + std::to_string(int(r)));
+  return cache.emplace(key, m).first->second;
+}
+
+int device_sms() {
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
+}  // namespace kh

@@ -1,0 +1,76 @@
+"""Attention of f16 plans on the tensor-core path, through the C ABI, against the float64
+reference of the reference's own attention test (tests/wasm_plan.test.ts:299-333): batches of
+sequences packed into shared 128-row tiles, prefix masks with NaN-poisoned padding rows (they
+must never enter a sum), masked query rows exactly zero, sliding windows, head dimensions 32 and
+64, sequences longer than one 128-key tile."""
+import numpy as np
+import pytest
+
+from kat_cases import attention_ref, prefix_mask
+
+pytestmark = pytest.mark.gpu
+
+
+def run_attention(qkv16, mask, L, B, H, D, scale, window, rows, op="mbflash"):
+    from kleinhirn_b200.backend import CudaBackend
+    hd = H * D
+    ops = [{"name": "attn", "kernel": op, "constants": {"L": L, "H": H, "D": D, "SCALE": scale, "WINDOW": window,
+                                                         "ROWS": B * L},
+            "bind": ["qkv", "mask", "ctx"], "dispatch": [H, "rows"]}]
+    plan = {"f16": True, "length": L, "batch": B, "markers": 0, "embeddingSize": 1,
+            "buffers": [{"id": "qkv", "bytes": 2 * B * L * 3 * hd, "usage": "rw"},
+                        {"id": "mask", "bytes": 4 * B * L, "usage": "rw"},
+                        {"id": "ctx", "bytes": 2 * B * L * hd, "usage": "rw"}],
+            "segments": [{"name": "s", "prefix": "", "ops": ops}], "inputs": {"embeddings": "mask", "mask": "mask"},
+            "output": {"buffer": "ctx", "bytes": 2 * B * L * hd, "dtype": "storage", "rows": B * L * hd, "cols": 1},
+            "captureSlots": 0, "captureSlotBytes": 0}
+    be = CudaBackend()
+    r = be.runner(plan)
+    r.write_buffer("qkv", qkv16)
+    r.write_buffer("mask", mask)
+    r.run(rows)
+    out = r.read_buffer("ctx", 2 * rows * hd).view(np.float16).astype(np.float64)
+    r.destroy()
+    be.dispose()
+    return out
+
+
+@pytest.mark.parametrize("D", [32, 64])
+@pytest.mark.parametrize("L,lens,window", [
+    (50, [50, 17, 33], 0),         # three sequences in one 128-row tile
+    (300, [300, 129], 0),          # several key tiles, a sequence across tiles
+    (200, [200, 150, 7, 61], 16),  # windowed layers
+    (512, [512], 0),
+    (96, [96, 1, 90, 64, 30], 5),
+])
+def test_packed_attention_f16(D, L, lens, window):
+    B, H = len(lens), 2
+    hd = H * D
+    rng = np.random.default_rng(L + D + window)
+    qkv = (rng.standard_normal(B * L * 3 * hd) * 1.5).astype(np.float16)
+    mask = prefix_mask(L, lens)
+    for r in range(B * L):
+        if not mask[r]:
+            qkv[r * 3 * hd:(r + 1) * 3 * hd] = np.nan
+    rows = lens[0] if B == 1 else B * L
+    scale = D ** -0.5
+    want = attention_ref(qkv.astype(np.float32), mask, L, B, H, D, scale, window, rows)
+    got = run_attention(qkv, mask, L, B, H, D, scale, window, rows)
+    keep = np.repeat(mask[:rows] > 0, hd)
+    assert np.all(got[~keep] == 0), "masked query rows must be exactly zero"
+    err = np.abs(got[keep] - want[keep])
+    tol = 4e-3 + 1e-2 * np.abs(want[keep])
+    assert np.all(err <= tol), f"worst {err.max()} at {int(np.argmax(err - tol))}"
+
+
+def test_single_call_rows_below_bucket():
+    """B = 1 with rows < L: only the real rows exist; stale rows past them are never read."""
+    L, H, D = 128, 12, 64
+    hd = H * D
+    rng = np.random.default_rng(9)
+    qkv = rng.standard_normal(L * 3 * hd).astype(np.float16)
+    qkv[77 * 3 * hd:] = np.nan
+    mask = prefix_mask(L, [77])
+    want = attention_ref(qkv.astype(np.float32), mask, L, 1, H, D, D ** -0.5, 0, 77)
+    got = run_attention(qkv, mask, L, 1, H, D, D ** -0.5, 0, 77)
+    assert np.allclose(got, want, atol=4e-3, rtol=1e-2), np.abs(got - want).max()
