@@ -9,25 +9,27 @@
 // keys. Masked value rows never enter a sum (they are zeroed before the PV product, as attpv.wgsl
 // loads them as zero).
 //
-// Work: one CTA per (packed tile of 128 consecutive packed rows, head). Short sequences share a
-// tile; a pair of rows from different sequences is masked. The keys of a tile are the packed rows
-// of every sequence its rows belong to (clamped to +-WINDOW around the tile on windowed layers),
-// in tiles of 128. 192 threads:
-//   warp 0     TMA: the Q tile once, K tiles (2 stages), V tiles (1 stage) from the qkv rows;
+// Work: one CTA per (packed tile of 128 consecutive packed rows, group of HG heads). Short
+// sequences share a tile; a pair of rows from different sequences is masked. The keys of a tile
+// are the packed rows of every sequence its rows belong to (clamped to +-WINDOW around the tile
+// on windowed layers), in tiles of 128; which of them are present and unmasked is computed once
+// per CTA as bit masks. The CTA walks (head, key tile) items in order, 192 threads:
+//   warp 0     TMA: Q of each head, K and V of each item, into rings that run ahead across heads;
 //   warp 1     one thread issues S = Q K^T (M 128, N 128 keys, K = D) into TMEM columns
-//              [0, 128) and O_j = P_j V_j (M 128, N = D, K 128 keys, V as an MN-major operand)
-//              into TMEM columns [128, 128 + D);
+//              [0, 128) and O = P V (M 128, N = D, K 128 keys, V as an MN-major operand) into
+//              TMEM columns [128, 128 + D); the next item's S is issued as soon as the softmax
+//              has read the current one, before the current PV;
 //   warps 2-5  softmax, one thread per query row (TMEM lane): scores in the log2 domain, running
-//              max and sum, P_j in f16 into shared memory (128-byte swizzled K-major rows), then
-//              the context row accumulated in registers: o = o * exp2(m_old - m_new) + O_j.
-// Two CTAs share an SM (256 TMEM columns and < 114 KB of shared memory each).
+//              max and sum, P in f16 into shared memory (128-byte swizzled K-major rows), then
+//              the context row accumulated in registers: o = o * exp2(m_old - m_new) + O.
+// Two CTAs share an SM (256 TMEM columns and <= 102 KB of shared memory each).
 
 #include <algorithm>
 
 #include "attn_tc.h"
+#include "runtime.h"
 #include "sm100.cuh"
 #include "tmap.h"
-#include "runtime.h"
 
 namespace kh {
 
@@ -39,19 +41,23 @@ constexpr int TQ = 128;
 constexpr int TKEYS = 128;
 constexpr int THREADS = 192;
 constexpr uint32_t TMEM_COLS = 256;
+constexpr int MAXKT = 160;  // key tiles of one CTA: sequences up to 10,000 rows
 
 template <int D>
 struct Cfg {
-  static constexpr int ROW_BYTES = D * 2;          // one q / k / v row: the swizzle width
-  static constexpr int TILE = 128 * ROW_BYTES;     // one 128-row tile
+  static constexpr int ROW_BYTES = D * 2;   // one q / k / v row: the swizzle width
+  static constexpr int TILE = 128 * ROW_BYTES;
+  static constexpr int QS = D == 32 ? 2 : 1;  // Q buffers
+  static constexpr int KS = 2;                // K stages
+  static constexpr int VS = D == 32 ? 2 : 1;  // V stages
   static constexpr int Q_OFF = 0;
-  static constexpr int K_OFF = TILE;               // 2 stages
-  static constexpr int V_OFF = 3 * TILE;
-  static constexpr int P_OFF = 4 * TILE;           // 2 blocks of 128 rows x 64 keys, 16 KB each
-  static constexpr int META_OFF = P_OFF + 32768;   // key sequence, mask, position: 3 x 128 words
-  static constexpr int BAR_OFF = META_OFF + 3 * 512;
+  static constexpr int K_OFF = Q_OFF + QS * TILE;
+  static constexpr int V_OFF = K_OFF + KS * TILE;
+  static constexpr int P_OFF = V_OFF + VS * TILE;  // 2 blocks of 128 rows x 64 keys, 16 KB each
+  static constexpr int BITS_OFF = P_OFF + 32768;   // present-and-unmasked / masked-key bits
+  static constexpr int BAR_OFF = BITS_OFF + 2 * MAXKT * 4 * 4;
   static constexpr int USED = BAR_OFF + 256;
-  // at least ~100 KB so that no more than two CTAs (2 x 256 TMEM columns) share an SM
+  // at least 100 KB so that no more than two CTAs (2 x 256 TMEM columns) share an SM
   static constexpr int SMEM = (USED + 1024 > 102400 ? USED + 1024 : 102400);
   static constexpr uint64_t LAYOUT = D == 64 ? 2ull : 4ull;  // 128- or 64-byte swizzle
   static constexpr uint64_t SBO = (8 * ROW_BYTES) >> 4;       // 8-row group stride, 16-byte units
@@ -62,10 +68,9 @@ struct Params {
   const int32_t* seq_start;
   const int32_t* seq_len;
   const int32_t* row_seq;
-  const int32_t* row_pos;
   const int32_t* ptiles;
   __half* ctx;
-  int H, T, window;
+  int H, HG, T, window;
   float scale_log2;  // SCALE * log2(e)
 };
 
@@ -74,10 +79,6 @@ __device__ __forceinline__ uint64_t desc_rows(const void* smem) {
   const uint64_t addr = smem_u32(smem);
   return ((addr >> 4) & 0x3FFFull) | (1ull << 16) | (Cfg<D>::SBO << 32) | (1ull << 46) | (Cfg<D>::LAYOUT << 61);
 }
-
-__device__ __forceinline__ void named_sync_softmax() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 template <int D>
 __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_constant__ CUtensorMap tm, const Params p) {
@@ -88,41 +89,44 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
   uint8_t* sK = smem + C::K_OFF;
   uint8_t* sV = smem + C::V_OFF;
   uint8_t* sP = smem + C::P_OFF;
-  int* kvalid = reinterpret_cast<int*>(smem + C::META_OFF);  // key row present and unmasked
-  volatile int* kholes = kvalid + 128;                         // per tile parity: a masked key exists
+  uint32_t* vbits = reinterpret_cast<uint32_t*>(smem + C::BITS_OFF);  // [tile][4]: key present, unmasked
+  uint32_t* hbits = vbits + MAXKT * 4;                                 // [tile][4]: key present, masked
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
-  uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;   // 2
-  uint64_t* k_empty = bars + 3;  // 2
-  uint64_t* v_full = bars + 5;
-  uint64_t* v_empty = bars + 6;
-  uint64_t* s_full = bars + 7;
-  uint64_t* s_empty = bars + 8;
-  uint64_t* p_full = bars + 9;
-  uint64_t* o_full = bars + 10;
-  uint64_t* drain = bars + 11;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* q_full = bars;       // 2
+  uint64_t* q_empty = bars + 2;  // 2
+  uint64_t* k_full = bars + 4;   // 2
+  uint64_t* k_empty = bars + 6;  // 2
+  uint64_t* v_full = bars + 8;   // 2
+  uint64_t* v_empty = bars + 10; // 2
+  uint64_t* s_full = bars + 12;
+  uint64_t* s_empty = bars + 13;
+  uint64_t* p_full = bars + 14;
+  uint64_t* o_full = bars + 15;
+  uint64_t* drain = bars + 16;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 17);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile = blockIdx.x, h = blockIdx.y;
-  const int H = p.H;
+  const int tile = blockIdx.x;
+  const int H = p.H, HG = p.HG, hg0 = blockIdx.y * HG;
   const int q0 = p.ptiles[3 * tile];
   int kstart = p.ptiles[3 * tile + 1], kend = p.ptiles[3 * tile + 2];
   if (p.window > 0) {
     kstart = max(kstart, q0 - p.window);
     kend = min(kend, q0 + TQ + p.window);
   }
-  const int nkt = (kend - kstart + TKEYS - 1) / TKEYS;
+  const int nkt = min((kend - kstart + TKEYS - 1) / TKEYS, MAXKT);
+  const int NI = HG * nkt;  // (head, key tile) items
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
     for (int s = 0; s < 2; ++s) {
+      mbar_init(&q_full[s], 1);
+      mbar_init(&q_empty[s], 1);
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
-    mbar_init(v_full, 1);
-    mbar_init(v_empty, 1);
     mbar_init(s_full, 1);
     mbar_init(s_empty, 128);
     mbar_init(p_full, 128);
@@ -141,67 +145,85 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
   if (warp == 0) {
     if (lane == 0) {
       bool ok = true;
-      uint32_t pend_k = 0, pend_v = 0;  // last issued parity per K stage / the V stage, bit 2: issued
-      mbar_arrive_expect_tx(q_full, C::TILE);
-      tma_load_2d(sQ, &tm, q_full, h * D, q0);
-      auto load_k = [&](int j) {
-        const int s = j & 1;
-        if (*abort_flag || !mbar_wait(&k_empty[s], ((j >> 1) & 1) ^ 1, 21)) return false;
-        mbar_arrive_expect_tx(&k_full[s], C::TILE);
-        tma_load_2d(sK + s * C::TILE, &tm, &k_full[s], (H + h) * D, kstart + j * TKEYS);
-        pend_k = (pend_k & ~(3u << (2 * s))) | ((4u | uint32_t((j >> 1) & 1)) << (2 * s));
-        return true;
-      };
-      ok = load_k(0);
-      for (int j = 0; j < nkt && ok; ++j) {
-        if (j + 1 < nkt && !load_k(j + 1)) ok = false;
-        if (!ok || *abort_flag || !mbar_wait(v_empty, (j & 1) ^ 1, 22)) {
-          ok = false;
-          break;
+      // issued loads not yet known complete: parity per ring slot (bit 2 = issued)
+      uint32_t pend_q = 0, pend_k = 0, pend_v = 0;
+      for (int it = 0; it < NI && ok; ++it) {
+        const int hh = it / nkt, j = it - hh * nkt, h = hg0 + hh;
+        const int y = kstart + j * TKEYS;
+        if (j == 0) {
+          const int s = hh % C::QS;
+          const uint32_t u = uint32_t(hh / C::QS);
+          if (*abort_flag || !mbar_wait(&q_empty[s], (u & 1) ^ 1, 20)) { ok = false; break; }
+          mbar_arrive_expect_tx(&q_full[s], C::TILE);
+          tma_load_2d(sQ + s * C::TILE, &tm, &q_full[s], h * D, q0);
+          pend_q = (pend_q & ~(7u << (3 * s))) | ((4u | (u & 1)) << (3 * s));
         }
-        mbar_arrive_expect_tx(v_full, C::TILE);
-        tma_load_2d(sV, &tm, v_full, (2 * H + h) * D, kstart + j * TKEYS);
-        pend_v = 4u | uint32_t(j & 1);
+        {
+          const int s = it % C::KS;
+          const uint32_t u = uint32_t(it / C::KS);
+          if (*abort_flag || !mbar_wait(&k_empty[s], (u & 1) ^ 1, 21)) { ok = false; break; }
+          mbar_arrive_expect_tx(&k_full[s], C::TILE);
+          tma_load_2d(sK + s * C::TILE, &tm, &k_full[s], (H + h) * D, y);
+          pend_k = (pend_k & ~(7u << (3 * s))) | ((4u | (u & 1)) << (3 * s));
+        }
+        {
+          const int s = it % C::VS;
+          const uint32_t u = uint32_t(it / C::VS);
+          if (*abort_flag || !mbar_wait(&v_empty[s], (u & 1) ^ 1, 22)) { ok = false; break; }
+          mbar_arrive_expect_tx(&v_full[s], C::TILE);
+          tma_load_2d(sV + s * C::TILE, &tm, &v_full[s], (2 * H + h) * D, y);
+          pend_v = (pend_v & ~(7u << (3 * s))) | ((4u | (u & 1)) << (3 * s));
+        }
       }
       if (!ok) {
         *abort_flag = 1;
-        mbar_wait(q_full, 0, 31);
-        for (int s = 0; s < 2; ++s)
-          if ((pend_k >> (2 * s)) & 4u) mbar_wait(&k_full[s], (pend_k >> (2 * s)) & 1u, 32);
-        if (pend_v & 4u) mbar_wait(v_full, pend_v & 1u, 33);
+        // every copy this thread issued lands before the CTA ends
+        for (int s = 0; s < 2; ++s) {
+          if ((pend_q >> (3 * s)) & 4u) mbar_wait(&q_full[s], (pend_q >> (3 * s)) & 1u, 31);
+          if ((pend_k >> (3 * s)) & 4u) mbar_wait(&k_full[s], (pend_k >> (3 * s)) & 1u, 32);
+          if ((pend_v >> (3 * s)) & 4u) mbar_wait(&v_full[s], (pend_v >> (3 * s)) & 1u, 33);
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc_s = idesc_f16(128, TKEYS);
       const uint32_t idesc_o = idesc_f16(128, D) | (1u << 16);  // B (V) MN-major
-      bool ok = mbar_wait(q_full, 0, 23) && !*abort_flag;
-      const uint64_t dq = desc_rows<D>(sQ);
-      for (int j = 0; j < nkt && ok; ++j) {
-        const int s = j & 1;
-        if (*abort_flag || !mbar_wait(&k_full[s], (j >> 1) & 1, 24) || !mbar_wait(s_empty, (j & 1) ^ 1, 25)) {
-          ok = false;
-          break;
-        }
+      bool ok = true;
+      auto issue_s = [&](int it) -> bool {
+        const int hh = it / nkt, j = it - hh * nkt;
+        const int qs = hh % C::QS, ks = it % C::KS;
+        if (j == 0 && !mbar_wait(&q_full[qs], uint32_t(hh / C::QS) & 1, 23)) return false;
+        if (*abort_flag || !mbar_wait(&k_full[ks], uint32_t(it / C::KS) & 1, 24)) return false;
+        if (*abort_flag || !mbar_wait(s_empty, uint32_t(it & 1) ^ 1, 25)) return false;
         fence_after_sync();
-        const uint64_t dk = desc_rows<D>(sK + s * C::TILE);
+        const uint64_t dq = desc_rows<D>(sQ + qs * C::TILE);
+        const uint64_t dk = desc_rows<D>(sK + ks * C::TILE);
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) mma_f16(tmem, dq + uint64_t(2 * k), dk + uint64_t(2 * k), idesc_s, k ? 1u : 0u);
         mma_commit(s_full);
-        mma_commit(&k_empty[s]);
-        if (*abort_flag || !mbar_wait(p_full, j & 1, 26) || !mbar_wait(v_full, j & 1, 27)) {
+        mma_commit(&k_empty[ks]);
+        if (j == nkt - 1) mma_commit(&q_empty[qs]);
+        return true;
+      };
+      ok = NI > 0 && issue_s(0);
+      for (int it = 0; it < NI && ok; ++it) {
+        if (it + 1 < NI && !issue_s(it + 1)) { ok = false; break; }
+        const int vs = it % C::VS;
+        if (*abort_flag || !mbar_wait(p_full, uint32_t(it & 1), 26) ||
+            !mbar_wait(&v_full[vs], uint32_t(it / C::VS) & 1, 27)) {
           ok = false;
           break;
         }
         fence_after_sync();
-        const uint64_t dv = desc_rows<D>(sV);
+        const uint64_t dv = desc_rows<D>(sV + vs * C::TILE);
 #pragma unroll
         for (int kk = 0; kk < TKEYS / 16; ++kk) {
           const uint64_t dp = desc_rows<64>(sP + (kk >> 2) * 16384) + uint64_t(2 * (kk & 3));
           mma_f16(tmem + 128, dp, dv + uint64_t(2 * D * kk), idesc_o, kk ? 1u : 0u);
         }
         mma_commit(o_full);
-        mma_commit(v_empty);
+        mma_commit(&v_empty[vs]);
       }
       if (!ok) {
         *abort_flag = 1;
@@ -213,6 +235,19 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
     const int quarter = warp & 3;
     const int r_local = quarter * 32 + lane;  // query row = TMEM lane
     const int st = threadIdx.x - 64;          // key row this thread prepares
+    const int sw = st >> 5;                   // its word of a key tile's bit masks
+    // which key rows of every key tile are present and unmasked (computed once for all heads)
+    for (int j = 0; j < nkt; ++j) {
+      const int kk = kstart + j * TKEYS + st;
+      const bool have = kk < kend && kk < p.T;
+      const bool valid = have && p.mask[kk] > 0.5f;
+      const uint32_t vb = __ballot_sync(0xffffffffu, valid);
+      const uint32_t hb = __ballot_sync(0xffffffffu, have && !valid);
+      if (lane == 0) {
+        vbits[j * 4 + sw] = vb;
+        hbits[j * 4 + sw] = hb;
+      }
+    }
     const int row = q0 + r_local;
     const bool in_range = row < p.T;
     const bool qvalid = in_range && p.mask[row] > 0.5f;
@@ -227,132 +262,120 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
         hi = min(hi, row + p.window + 1);
       }
     }
+    named_bar(1, 128);
     const uint32_t trow = tmem + (uint32_t(quarter * 32) << 16);
-    float m = -3.40282346638528859812e38f, l = 0.f;
-    float o[D];
-#pragma unroll
-    for (int d = 0; d < D; ++d) o[d] = 0.f;
     bool ok = true;
-    for (int j = 0; j < nkt; ++j) {
-      const int k0 = kstart + j * TKEYS;
-      if (st == 0) kholes[j & 1] = 0;
-      named_sync_softmax();
-      {
-        const int kk = k0 + st;
-        const bool have = kk < kend && kk < p.T;
-        const bool valid = have && p.mask[kk] > 0.5f;
-        kvalid[st] = valid ? 1 : 0;
-        if (have && !valid) kholes[j & 1] = 1;
-      }
-      named_sync_softmax();
-      const bool holes = kholes[j & 1] != 0;
-      const int clo = min(max(lo - k0, 0), TKEYS), chi = min(max(hi - k0, 0), TKEYS);
-      if (*abort_flag || !mbar_wait(s_full, j & 1, 41)) {
-        ok = false;
-        break;
-      }
-      fence_after_sync();
-      // pass 1: the row maximum of the kept raw scores
-      float mraw = -3.40282346638528859812e38f;
-#pragma unroll 1
-      for (int c4 = 0; c4 < 4; ++c4) {
-        const bool need = c4 * 32 < chi && c4 * 32 + 32 > clo;
-        if (!__any_sync(0xffffffffu, need)) continue;
-        uint32_t r[32];
-        tmem_ld32(trow + c4 * 32, r);
-        tmem_ld_wait();
-        if (!need) continue;
+    for (int hh = 0; hh < HG && ok; ++hh) {
+      float m = -3.40282346638528859812e38f, l = 0.f;
+      float o[D];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int c = c4 * 32 + i;
-          const bool keep = c >= clo && c < chi && (!holes || kvalid[c]);
-          if (keep) mraw = fmaxf(mraw, __uint_as_float(r[i]));
-        }
-      }
-      const float mx = fmaxf(m, mraw * p.scale_log2);
-      const float corr = exp2f(m - mx);
-      l *= corr;
-      // pass 2: p = exp2(s scale log2e - max) in f16, into this row of P (128-byte swizzled)
+      for (int d = 0; d < D; ++d) o[d] = 0.f;
+      for (int j = 0; j < nkt; ++j) {
+        const int it = hh * nkt + j;
+        const int k0 = kstart + j * TKEYS;
+        const bool holes = (hbits[j * 4] | hbits[j * 4 + 1] | hbits[j * 4 + 2] | hbits[j * 4 + 3]) != 0;
+        const int clo = min(max(lo - k0, 0), TKEYS), chi = min(max(hi - k0, 0), TKEYS);
+        if (*abort_flag || !mbar_wait(s_full, uint32_t(it & 1), 41)) { ok = false; break; }
+        fence_after_sync();
+        // pass 1: the row maximum of the kept raw scores
+        float mraw = -3.40282346638528859812e38f;
 #pragma unroll 1
-      for (int c4 = 0; c4 < 4; ++c4) {
-        const bool need = c4 * 32 < chi && c4 * 32 + 32 > clo;
-        uint32_t packed[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) packed[i] = 0u;
-        if (__any_sync(0xffffffffu, need)) {
+        for (int c4 = 0; c4 < 4; ++c4) {
+          const bool need = c4 * 32 < chi && c4 * 32 + 32 > clo;
+          if (!__any_sync(0xffffffffu, need)) continue;
           uint32_t r[32];
           tmem_ld32(trow + c4 * 32, r);
           tmem_ld_wait();
-          if (need) {
+          if (!need) continue;
+          const uint32_t vw = holes ? vbits[j * 4 + c4] : 0xffffffffu;
 #pragma unroll
-            for (int i = 0; i < 32; i += 2) {
-              float pv[2];
-#pragma unroll
-              for (int e = 0; e < 2; ++e) {
-                const int c = c4 * 32 + i + e;
-                const bool keep = c >= clo && c < chi && (!holes || kvalid[c]);
-                pv[e] = keep ? exp2f(fmaf(__uint_as_float(r[i + e]), p.scale_log2, -mx)) : 0.f;
-                l += pv[e];
-              }
-              __half2 hv = __floats2half2_rn(pv[0], pv[1]);
-              packed[i / 2] = *reinterpret_cast<uint32_t*>(&hv);
-            }
+          for (int i = 0; i < 32; ++i) {
+            const int c = c4 * 32 + i;
+            if (c >= clo && c < chi && ((vw >> i) & 1u)) mraw = fmaxf(mraw, __uint_as_float(r[i]));
           }
         }
-        // keys c4*32 .. +31: block c4/2, 16-byte chunks 4 (c4 % 2) .. +3 of this row, swizzled
-        uint8_t* prow = sP + (c4 >> 1) * 16384 + r_local * 128;
+        const float mx = fmaxf(m, mraw * p.scale_log2);
+        const float corr = exp2f(m - mx);
+        l *= corr;
+        // pass 2: p = exp2(s scale log2e - max) in f16, into this row of P (128-byte swizzled)
+#pragma unroll 1
+        for (int c4 = 0; c4 < 4; ++c4) {
+          const bool need = c4 * 32 < chi && c4 * 32 + 32 > clo;
+          uint32_t packed[16];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int ch = (c4 & 1) * 4 + q;
-          *reinterpret_cast<uint4*>(prow + ((ch ^ (r_local & 7)) * 16)) =
-              make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+          for (int i = 0; i < 16; ++i) packed[i] = 0u;
+          if (__any_sync(0xffffffffu, need)) {
+            uint32_t r[32];
+            tmem_ld32(trow + c4 * 32, r);
+            tmem_ld_wait();
+            if (need) {
+              const uint32_t vw = holes ? vbits[j * 4 + c4] : 0xffffffffu;
+#pragma unroll
+              for (int i = 0; i < 32; i += 2) {
+                float pv[2];
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                  const int c = c4 * 32 + i + e;
+                  const bool keep = c >= clo && c < chi && ((vw >> (i + e)) & 1u);
+                  pv[e] = keep ? exp2f(fmaf(__uint_as_float(r[i + e]), p.scale_log2, -mx)) : 0.f;
+                  l += pv[e];
+                }
+                __half2 hv = __floats2half2_rn(pv[0], pv[1]);
+                packed[i / 2] = *reinterpret_cast<uint32_t*>(&hv);
+              }
+            }
+          }
+          // keys c4*32 .. +31: block c4/2, 16-byte chunks 4 (c4 % 2) .. +3 of this row, swizzled
+          uint8_t* prow = sP + (c4 >> 1) * 16384 + r_local * 128;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int ch = (c4 & 1) * 4 + q;
+            *reinterpret_cast<uint4*>(prow + ((ch ^ (r_local & 7)) * 16)) =
+                make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+          }
+        }
+        m = mx;
+        fence_before_sync();
+        mbar_arrive(s_empty);
+        // value rows of masked or absent keys become zero before the PV product
+        const int vs = it % C::VS;
+        if (*abort_flag || !mbar_wait(&v_full[vs], uint32_t(it / C::VS) & 1, 42)) { ok = false; break; }
+        if (!((vbits[j * 4 + sw] >> (st & 31)) & 1u)) {
+          uint4* vrow = reinterpret_cast<uint4*>(sV + vs * C::TILE + st * C::ROW_BYTES);
+#pragma unroll
+          for (int q = 0; q < C::ROW_BYTES / 16; ++q) vrow[q] = make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(p_full);
+        if (*abort_flag || !mbar_wait(o_full, uint32_t(it & 1), 43)) { ok = false; break; }
+        fence_after_sync();
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(trow + 128 + c * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[c * 32 + i] = fmaf(o[c * 32 + i], corr, __uint_as_float(r[i]));
         }
       }
-      m = mx;
-      fence_before_sync();
-      mbar_arrive(s_empty);
-      // value rows of masked or absent keys become zero before the PV product
-      if (*abort_flag || !mbar_wait(v_full, j & 1, 42)) {
-        ok = false;
-        break;
-      }
-      if (!kvalid[st]) {
-        uint4* vrow = reinterpret_cast<uint4*>(sV + st * C::ROW_BYTES);
+      if (!ok) break;
+      if (in_range) {
+        // a masked query row, or one without a kept key, is exactly zero (select, not multiply)
+        const bool live = qvalid && l > 0.f;
+        const float inv = live ? 1.0f / l : 0.f;
+        uint4* dst = reinterpret_cast<uint4*>(p.ctx + int64_t(row) * H * D + int64_t(hg0 + hh) * D);
 #pragma unroll
-        for (int q = 0; q < C::ROW_BYTES / 16; ++q) vrow[q] = make_uint4(0, 0, 0, 0);
-      }
-      fence_proxy_async();
-      mbar_arrive(p_full);
-      if (*abort_flag || !mbar_wait(o_full, j & 1, 43)) {
-        ok = false;
-        break;
-      }
-      fence_after_sync();
+        for (int q = 0; q < D / 8; ++q) {
+          __half2 hv[4];
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(trow + 128 + c * 32, r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[c * 32 + i] = fmaf(o[c * 32 + i], corr, __uint_as_float(r[i]));
+          for (int e = 0; e < 4; ++e)
+            hv[e] = live ? __floats2half2_rn(o[q * 8 + 2 * e] * inv, o[q * 8 + 2 * e + 1] * inv)
+                         : __floats2half2_rn(0.f, 0.f);
+          dst[q] = *reinterpret_cast<uint4*>(hv);
+        }
       }
     }
     if (!ok) *abort_flag = 1;
-    if (in_range) {
-      // a masked query row, or one without a kept key, is exactly zero (select, not multiply)
-      const bool live = ok && qvalid && l > 0.f;
-      const float inv = live ? 1.0f / l : 0.f;
-      uint4* dst = reinterpret_cast<uint4*>(p.ctx + int64_t(row) * H * D + int64_t(h) * D);
-#pragma unroll
-      for (int q = 0; q < D / 8; ++q) {
-        __half2 hv[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          hv[e] = live ? __floats2half2_rn(o[q * 8 + 2 * e] * inv, o[q * 8 + 2 * e + 1] * inv)
-                       : __floats2half2_rn(0.f, 0.f);
-        dst[q] = *reinterpret_cast<uint4*>(hv);
-      }
-    }
   }
   fence_before_sync();
   __syncthreads();
@@ -360,6 +383,12 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
     fence_after_sync();
     tmem_free(tmem, TMEM_COLS);
   }
+}
+
+int heads_per_cta(int H) {
+  for (int g = 4; g > 1; --g)
+    if (H % g == 0) return g;
+  return 1;
 }
 
 template <int D>
@@ -376,14 +405,14 @@ void launch_tc(const AttnArgs& a, const SeqTable& seq, int T, cudaStream_t st) {
   p.seq_start = seq.start;
   p.seq_len = seq.len;
   p.row_seq = seq.row_seq;
-  p.row_pos = seq.row_pos;
   p.ptiles = seq.ptiles;
   p.ctx = static_cast<__half*>(a.ctx);
   p.H = a.H;
+  p.HG = heads_per_cta(a.H);
   p.T = T;
   p.window = a.window;
   p.scale_log2 = a.scale * 1.4426950408889634f;
-  dim3 grid(seq.nptiles, a.H);
+  dim3 grid(seq.nptiles, a.H / p.HG);
   attn_tc_kernel<D><<<grid, THREADS, Cfg<D>::SMEM, st>>>(tm, p);
 }
 
@@ -391,16 +420,19 @@ void launch_tc(const AttnArgs& a, const SeqTable& seq, int T, cudaStream_t st) {
 
 int attention_tile_q(bool) { return 64; }
 
-bool attention_tc_supported(bool f16, const AttnArgs& a) { return f16 && !a.rel && (a.D == 64 || a.D == 32); }
+bool attention_tc_supported(bool f16, const AttnArgs& a) {
+  // the key rows of one packed tile must fit the CTA's key-tile masks
+  return f16 && !a.rel && (a.D == 64 || a.D == 32) && a.L <= (MAXKT * TKEYS - TQ) / 2;
+}
 
 void launch_attention(bool f16, const AttnArgs& a, const SeqTable& seq, cudaStream_t st) {
-  if (seq.nptiles <= 0) return;
+  if (seq.nptiles <= 0 && seq.ntiles <= 0) return;
   if (!attention_tc_supported(f16, a)) {
     launch_attention_simt(f16, a, seq, st);
     return;
   }
-  // packed rows of the launch: the last packed tile ends at T
-  const int T = a.rows;
+  if (seq.nptiles <= 0) return;
+  const int T = a.rows;  // packed rows of the launch: the last packed tile ends at T
   if (a.D == 64) launch_tc<64>(a, seq, T, st);
   else launch_tc<32>(a, seq, T, st);
 }

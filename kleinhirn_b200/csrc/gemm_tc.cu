@@ -2,21 +2,24 @@
 // (the activations), W [N, K] f16 row-major (PyTorch [out, in] weights, as the reference stores
 // them, src/convert/names.ts:5), f32 accumulation in TMEM.
 //
-// One persistent CTA per SM, 192 threads in three roles:
-//   warp 0      TMA producer: 128 x 64 tiles of A and BN x 64 tiles of W into a ring of STAGES
+// One persistent CTA per SM, 320 threads in three roles:
+//   warp 0      TMA producer: 128 x 64 tiles of A and 128 x 64 tiles of W into a ring of STAGES
 //               shared-memory stages (128-byte swizzle), completion on per-stage mbarriers;
-//   warp 1      MMA issuer: one thread issues tcgen05.mma kind::f16 (M 128, N BN, K 16) into
+//   warp 1      MMA issuer: one thread issues tcgen05.mma kind::f16 (M 128, N 128, K 16) into
 //               one of two TMEM accumulators, commits each stage back to the producer and each
 //               finished tile to the epilogue;
-//   warps 2-5   epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes 32 (w % 4) ..),
-//               bias, activation and the fused follow-up op, f16 store.
+//   warps 2-9   epilogue, two warpgroups: warpgroup g takes accumulator columns [64 g, 64 g + 64)
+//               (warp w reads TMEM lanes 32 (w % 4) ..); bias, activation and the fused
+//               follow-up op in registers, the f16 result into a swizzled shared-memory tile,
+//               written out by one TMA store per warpgroup (rows and columns past M and N are
+//               clipped by the tensor map).
 // Tiles run n-fastest so the CTAs working at the same time share rows of A in L2.
 //
 // Epilogues reproduce the reference's storage rounding exactly (every value the reference
 // stores in the plan's f16 buffer is rounded to f16 here before it is used again):
 //   plain     C = f16(act(acc + bias))                              (matmul.wgsl / mmtile.wgsl)
 //   residual  C = f16(C + f16(acc + bias))                          (matmul, then add.wgsl)
-//   geglu     W rows interleaved per 64 columns: C[r, j] = f16(gelu(f16(a + ba)) * f16(b + bb))
+//   geglu     W rows interleaved per 64: C[r, j] = f16(gelu(f16(a + ba)) * f16(b + bb))
 //                                                                   (matmul, then geglu.wgsl)
 //   rope      q and k head blocks rotated with the f32 cos / sin table row of the local position:
 //             C = f16(x c - y s), f16(y c + x s) with x, y = f16(acc + bias) (matmul, then rope.wgsl)
@@ -39,26 +42,27 @@ using namespace sm100;
 constexpr int BM = 128;
 constexpr int BN = 128;
 constexpr int BK = 64;
-constexpr int STAGES = 6;
+constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BK * 2;
 constexpr int B_BYTES = BN * BK * 2;
-constexpr int THREADS = 192;
+constexpr int OUT_BYTES = 128 * 64 * 2;  // one warpgroup's staged output tile
+constexpr int THREADS = 320;
+constexpr int EPI_THREADS = 256;
 constexpr uint32_t TMEM_COLS = 2 * BN;
-constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + 1024 + 256;
+constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + 4 * OUT_BYTES + 1024 + 256;
 
 enum Epi { EPI_PLAIN = 0, EPI_RESIDUAL = 1, EPI_GEGLU = 2, EPI_ROPE = 3 };
 
 struct Params {
   int M, N, K;
   const __half* bias;
-  __half* C;
+  const __half* C;  // residual source (the output itself)
   int ldc;
   int act;
   int epi;
   const float* table;
   const int32_t* row_pos;
-  int D;          // rope head dimension
-  int rope_cols;  // columns of q and k (2 H D)
+  int rope_cols;  // columns of q and k (2 H D), heads of 64
 };
 
 __device__ __forceinline__ float gelu_as(float v) {
@@ -80,41 +84,65 @@ __device__ __forceinline__ float act_fn(float v, int act) {
 
 __device__ __forceinline__ float f16r(float v) { return __half2float(__float2half_rn(v)); }
 
-__device__ __forceinline__ void store32(__half* dst, const float (&v)[32]) {
-  uint4* d = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    __half2 h[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) h[e] = __floats2half2_rn(v[q * 8 + 2 * e], v[q * 8 + 2 * e + 1]);
-    d[q] = *reinterpret_cast<uint4*>(h);
-  }
-}
-
-__device__ __forceinline__ void load32(const __half* src, float (&v)[32]) {
+// 32 consecutive f16 values of a row (16-byte aligned) as f32
+__device__ __forceinline__ void load32h(const __half* src, float (&v)[32]) {
   const uint4* s = reinterpret_cast<const uint4*>(src);
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
-    uint4 u = s[q];
+    const uint4 u = s[q];
     const __half2* h = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      float2 f = __half22float2(h[e]);
+      const float2 f = __half22float2(h[e]);
       v[q * 8 + 2 * e] = f.x;
       v[q * 8 + 2 * e + 1] = f.y;
     }
   }
 }
 
-__device__ __forceinline__ float bias_at(const __half* b, int n) { return b ? __half2float(b[n]) : 0.0f; }
+__device__ __forceinline__ void bias32(const __half* b, int n, float (&v)[32]) {
+  if (b) {
+    load32h(b + n, v);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = 0.f;
+  }
+}
+
+// Row r of a staged tile with 128-byte rows (128-byte swizzle, the TMA layout of a 64-column
+// f16 box): the 16-byte chunks ch .. ch + 3 hold v[0 .. 31].
+__device__ __forceinline__ void stage32_sw128(uint8_t* tile, int r, int ch, const float (&v)[32]) {
+  uint8_t* row = tile + r * 128;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    __half2 h[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) h[e] = __floats2half2_rn(v[q * 8 + 2 * e], v[q * 8 + 2 * e + 1]);
+    *reinterpret_cast<uint4*>(row + (((ch + q) ^ (r & 7)) * 16)) = *reinterpret_cast<uint4*>(h);
+  }
+}
+
+// Row r of a staged tile with 64-byte rows (64-byte swizzle, a 32-column f16 box).
+__device__ __forceinline__ void stage32_sw64(uint8_t* tile, int r, const float (&v)[32]) {
+  uint8_t* row = tile + r * 64;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    __half2 h[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) h[e] = __floats2half2_rn(v[q * 8 + 2 * e], v[q * 8 + 2 * e + 1]);
+    *reinterpret_cast<uint4*>(row + ((q ^ ((r >> 1) & 3)) * 16)) = *reinterpret_cast<uint4*>(h);
+  }
+}
 
 __global__ void __launch_bounds__(THREADS, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmC, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint8_t* sOut = sB + STAGES * B_BYTES;  // [warpgroup][buffer] 16 KB tiles
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + 4 * OUT_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -134,13 +162,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 128);
+      mbar_init(&tempty[b], EPI_THREADS);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    prefetch_tmap(&tmC);
   }
   if (warp == 1) tmem_alloc(tmem_holder, TMEM_COLS);
   fence_before_sync();
@@ -222,7 +251,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
   } else {
-    const int q = warp & 3;  // TMEM lane quarter of this warp
+    const int q = warp & 3;          // TMEM lane quarter of this warp
+    const int g = (warp - 2) >> 2;   // warpgroup: accumulator columns [64 g, 64 g + 64)
+    const int r = q * 32 + lane;     // row of the tile
+    const bool leader = (warp == 2 + 4 * g) && lane == 0;
     int local = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
       const int buf = local & 1;
@@ -233,80 +265,89 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       fence_after_sync();
       const int mb = t / n_tiles, nb = t % n_tiles;
-      const int row = mb * BM + q * 32 + lane;
+      const int row = mb * BM + r;
       const bool live = row < p.M;
       const int n0 = nb * BN;
       const uint32_t taddr = tmem + (uint32_t(q * 32) << 16) + uint32_t(buf * BN);
+      uint8_t* stile = sOut + (g * 2 + buf) * OUT_BYTES;
+      // the TMA store that read this staging tile two tiles ago must be done with it
+      if (leader) bulk_wait_read<1>();
+      named_bar(1 + g, 128);
       if (p.epi == EPI_GEGLU) {
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          uint32_t ra[32], rb[32];
-          tmem_ld32(taddr + c * 32, ra);
-          tmem_ld32(taddr + 64 + c * 32, rb);
-          tmem_ld_wait();
-          const int g0 = nb * 64 + c * 32;
-          if (live && g0 < p.ldc) {
-            float v[32];
+        // output columns [nb 64 + 32 g, + 32): a from accumulator columns 32 g.., b from 64 + 32 g..
+        uint32_t ra[32], rb[32];
+        tmem_ld32(taddr + 32 * g, ra);
+        tmem_ld32(taddr + 64 + 32 * g, rb);
+        tmem_ld_wait();
+        fence_before_sync();
+        mbar_arrive(&tempty[buf]);  // the accumulator is read: the MMA may reuse it
+        float ba[32], bb[32], v[32];
+        bias32(p.bias, n0 + 32 * g, ba);
+        bias32(p.bias, n0 + 64 + 32 * g, bb);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const float a = f16r(__uint_as_float(ra[i]) + bias_at(p.bias, n0 + c * 32 + i));
-              const float b = f16r(__uint_as_float(rb[i]) + bias_at(p.bias, n0 + 64 + c * 32 + i));
-              v[i] = gelu_as(a) * b;
-            }
-            store32(p.C + int64_t(row) * p.ldc + g0, v);
-          }
+        for (int i = 0; i < 32; ++i) {
+          const float a = f16r(__uint_as_float(ra[i]) + ba[i]);
+          const float b = f16r(__uint_as_float(rb[i]) + bb[i]);
+          v[i] = gelu_as(a) * b;
         }
+        stage32_sw64(stile, r, v);
       } else {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; c += 2) {
-          uint32_t r0[32], r1[32];
-          tmem_ld32(taddr + c * 32, r0);
-          tmem_ld32(taddr + (c + 1) * 32, r1);
-          tmem_ld_wait();
-          const int n = n0 + c * 32;
-          if (!live || n >= p.N) continue;
-          float v[64];
+        const int nc = n0 + 64 * g;
+        uint32_t r0[32], r1[32];
+        tmem_ld32(taddr + 64 * g, r0);
+        tmem_ld32(taddr + 64 * g + 32, r1);
+        tmem_ld_wait();
+        fence_before_sync();
+        mbar_arrive(&tempty[buf]);  // the accumulator is read: the MMA may reuse it
+        float v0[32], v1[32];
+        bias32(p.bias, min(nc, p.N - 32), v0);
+        bias32(p.bias, min(nc + 32, p.N - 32), v1);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            v[i] = __uint_as_float(r0[i]) + bias_at(p.bias, n + i);
-            v[32 + i] = __uint_as_float(r1[i]) + bias_at(p.bias, n + 32 + i);
-          }
-          __half* dst = p.C + int64_t(row) * p.ldc + n;
-          if (p.epi == EPI_ROPE && n < p.rope_cols) {
-            // one 64-wide head (D == 64): rotate-half with the table row of the local position
-            const float* tb = p.table + int64_t(p.row_pos[row]) * 2 * 64;
-#pragma unroll
-            for (int d = 0; d < 32; ++d) {
-              const float x = f16r(v[d]), y = f16r(v[d + 32]);
-              const float cs = tb[d], sn = tb[64 + d];
-              v[d] = x * cs - y * sn;
-              v[d + 32] = y * cs + x * sn;
-            }
-          } else if (p.epi == EPI_RESIDUAL) {
-            float r[32];
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              load32(dst + h * 32, r);
-#pragma unroll
-              for (int i = 0; i < 32; ++i) v[h * 32 + i] = r[i] + f16r(v[h * 32 + i]);
-            }
-          } else if (p.act) {
-#pragma unroll
-            for (int i = 0; i < 64; ++i) v[i] = act_fn(v[i], p.act);
-          }
-          float lo[32], hi[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            lo[i] = v[i];
-            hi[i] = v[32 + i];
-          }
-          store32(dst, lo);
-          if (n + 32 < p.N) store32(dst + 32, hi);
+        for (int i = 0; i < 32; ++i) {
+          v0[i] += __uint_as_float(r0[i]);
+          v1[i] += __uint_as_float(r1[i]);
         }
+        if (p.epi == EPI_ROPE && nc < p.rope_cols) {
+          // one 64-wide head: rotate-half with the table row of the local position
+          const float* tb = p.table + int64_t(live ? p.row_pos[row] : 0) * 128;
+#pragma unroll
+          for (int d = 0; d < 32; ++d) {
+            const float x = f16r(v0[d]), y = f16r(v1[d]);
+            const float cs = tb[d], sn = tb[64 + d];
+            v0[d] = x * cs - y * sn;
+            v1[d] = y * cs + x * sn;
+          }
+        } else if (p.epi == EPI_RESIDUAL) {
+          float res[32];
+          if (live && nc < p.N) {
+            load32h(p.C + int64_t(row) * p.ldc + nc, res);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v0[i] = res[i] + f16r(v0[i]);
+          }
+          if (live && nc + 32 < p.N) {
+            load32h(p.C + int64_t(row) * p.ldc + nc + 32, res);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v1[i] = res[i] + f16r(v1[i]);
+          }
+        } else if (p.act) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            v0[i] = act_fn(v0[i], p.act);
+            v1[i] = act_fn(v1[i], p.act);
+          }
+        }
+        stage32_sw128(stile, r, 0, v0);
+        stage32_sw128(stile, r, 4, v1);
       }
-      fence_before_sync();
-      mbar_arrive(&tempty[buf]);
+      fence_proxy_async_smem();
+      named_bar(1 + g, 128);
+      if (leader) {
+        if (p.epi == EPI_GEGLU) tma_store_2d(&tmC, stile, nb * 64 + 32 * g, mb * BM);
+        else if (n0 + 64 * g < p.N) tma_store_2d(&tmC, stile, n0 + 64 * g, mb * BM);
+        bulk_commit();
+      }
     }
+    if (leader) bulk_wait<0>();
   }
   fence_before_sync();
   __syncthreads();
@@ -318,7 +359,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 }  // namespace
 
-bool gemm_tc_supported(int N, int K) { return N >= 32 && N % 32 == 0 && K % 8 == 0 && K >= 16; }
+bool gemm_tc_supported(int N, int K) { return N >= 64 && N % 64 == 0 && K % 8 == 0 && K >= 16; }
 bool gemm_tc_supported_geglu(int N, int K) { return N % 128 == 0 && gemm_tc_supported(N, K); }
 bool gemm_tc_supported_rope(int D) { return D == 64; }
 
@@ -364,6 +405,7 @@ DevTensor gemm_geglu_bias(Ctx* ctx, const std::string& name, int N) {
   return d;
 }
 
+
 void launch_gemm(Ctx* ctx, bool f16, const void* A, const void* W, const void* bias, void* C, int M, int N, int K,
                  int act, const GemmEpilogue& e, cudaStream_t st) {
   (void)ctx;
@@ -383,13 +425,12 @@ void launch_gemm(Ctx* ctx, bool f16, const void* A, const void* W, const void* b
   p.N = N;
   p.K = K;
   p.bias = static_cast<const __half*>(bias);
-  p.C = static_cast<__half*>(C);
+  p.C = static_cast<const __half*>(C);
   p.ldc = N;
   p.act = act;
   p.epi = EPI_PLAIN;
   p.table = nullptr;
   p.row_pos = nullptr;
-  p.D = 0;
   p.rope_cols = 0;
   if (e.kind == GemmEpilogue::Residual) {
     p.epi = EPI_RESIDUAL;
@@ -398,18 +439,21 @@ void launch_gemm(Ctx* ctx, bool f16, const void* A, const void* W, const void* b
     p.epi = EPI_GEGLU;
     p.ldc = N / 2;
   } else if (e.kind == GemmEpilogue::Rope) {
+    if (e.D != 64) throw PlanError("rope epilogue needs 64-wide heads");
     p.epi = EPI_ROPE;
     p.table = e.table;
     p.row_pos = e.row_pos;
-    p.D = e.D;
     p.rope_cols = 2 * e.H * e.D;
   }
   const CUtensorMap& ma = tensor_map_f16(A, uint64_t(M), uint64_t(K), uint64_t(K), BK, BM, 128);
   const CUtensorMap& mb = tensor_map_f16(W, uint64_t(N), uint64_t(K), uint64_t(K), BK, BN, 128);
+  const CUtensorMap& mc = p.epi == EPI_GEGLU
+                              ? tensor_map_f16(C, uint64_t(M), uint64_t(N / 2), uint64_t(N / 2), 32, 128, 64)
+                              : tensor_map_f16(C, uint64_t(M), uint64_t(N), uint64_t(N), 64, 128, 128);
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   static const int sms = device_sms();
   const int grid = std::min(tiles, sms);
-  gemm_tc_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(ma, mb, p);
+  gemm_tc_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(ma, mb, mc, p);
 }
 
 int tc_error_code() {
