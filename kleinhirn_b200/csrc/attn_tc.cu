@@ -277,8 +277,9 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
         const int clo = min(max(lo - k0, 0), TKEYS), chi = min(max(hi - k0, 0), TKEYS);
         if (*abort_flag || !mbar_wait(s_full, uint32_t(it & 1), 41)) { ok = false; break; }
         fence_after_sync();
-        // pass 1: the row maximum of the kept raw scores
-        float mraw = -3.40282346638528859812e38f;
+        // pass 1: the row maximum of the kept raw scores (four independent chains)
+        float mr[4] = {-3.40282346638528859812e38f, -3.40282346638528859812e38f, -3.40282346638528859812e38f,
+                       -3.40282346638528859812e38f};
 #pragma unroll 1
         for (int c4 = 0; c4 < 4; ++c4) {
           const bool need = c4 * 32 < chi && c4 * 32 + 32 > clo;
@@ -287,16 +288,22 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
           tmem_ld32(trow + c4 * 32, r);
           tmem_ld_wait();
           if (!need) continue;
-          const uint32_t vw = holes ? vbits[j * 4 + c4] : 0xffffffffu;
+          if (!holes && clo <= c4 * 32 && c4 * 32 + 32 <= chi) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int c = c4 * 32 + i;
-            if (c >= clo && c < chi && ((vw >> i) & 1u)) mraw = fmaxf(mraw, __uint_as_float(r[i]));
+            for (int i = 0; i < 32; ++i) mr[i & 3] = fmaxf(mr[i & 3], __uint_as_float(r[i]));
+          } else {
+            const uint32_t vw = holes ? vbits[j * 4 + c4] : 0xffffffffu;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int c = c4 * 32 + i;
+              if (c >= clo && c < chi && ((vw >> i) & 1u)) mr[i & 3] = fmaxf(mr[i & 3], __uint_as_float(r[i]));
+            }
           }
         }
+        const float mraw = fmaxf(fmaxf(mr[0], mr[1]), fmaxf(mr[2], mr[3]));
         const float mx = fmaxf(m, mraw * p.scale_log2);
-        const float corr = exp2f(m - mx);
-        l *= corr;
+        const float corr = ex2_approx(m - mx);
+        float ls[4] = {0.f, 0.f, 0.f, 0.f};
         // pass 2: p = exp2(s scale log2e - max) in f16, into this row of P (128-byte swizzled)
 #pragma unroll 1
         for (int c4 = 0; c4 < 4; ++c4) {
@@ -309,6 +316,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
             tmem_ld32(trow + c4 * 32, r);
             tmem_ld_wait();
             if (need) {
+              const bool whole = !holes && clo <= c4 * 32 && c4 * 32 + 32 <= chi;
               const uint32_t vw = holes ? vbits[j * 4 + c4] : 0xffffffffu;
 #pragma unroll
               for (int i = 0; i < 32; i += 2) {
@@ -316,9 +324,9 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
                   const int c = c4 * 32 + i + e;
-                  const bool keep = c >= clo && c < chi && ((vw >> (i + e)) & 1u);
-                  pv[e] = keep ? exp2f(fmaf(__uint_as_float(r[i + e]), p.scale_log2, -mx)) : 0.f;
-                  l += pv[e];
+                  const bool keep = whole || (c >= clo && c < chi && ((vw >> (i + e)) & 1u));
+                  pv[e] = keep ? ex2_approx(fmaf(__uint_as_float(r[i + e]), p.scale_log2, -mx)) : 0.f;
+                  ls[(i + e) & 3] += pv[e];
                 }
                 __half2 hv = __floats2half2_rn(pv[0], pv[1]);
                 packed[i / 2] = *reinterpret_cast<uint32_t*>(&hv);
@@ -334,6 +342,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
                 make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
           }
         }
+        l = l * corr + ((ls[0] + ls[1]) + (ls[2] + ls[3]));
         m = mx;
         fence_before_sync();
         mbar_arrive(s_empty);

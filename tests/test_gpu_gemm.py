@@ -77,9 +77,10 @@ def test_gemm_relu_silu(act):
     test_gemm_shapes(256, 384, 384, act)
 
 
-def test_residual_epilogue():
+@pytest.mark.parametrize("N", [384, 768])  # 128- and 256-wide tiles
+def test_residual_epilogue(N):
     """matmul (attnOut) followed by add (addA): x = f16(x + f16(A W^T + b))."""
-    M, N, K, L = 300, 384, 384, 300
+    M, K, L = 300, 384, 300
     rng = np.random.default_rng(1)
     A = (rng.standard_normal((M, K)) * 0.5).astype(np.float16)
     W = (rng.standard_normal((N, K)) * 0.05).astype(np.float16)
@@ -96,9 +97,10 @@ def test_residual_epilogue():
     assert_f16_close(got, want.reshape(-1), "residual")
 
 
-def test_geglu_epilogue():
+@pytest.mark.parametrize("I", [1152, 192])  # interleave groups of 128 and 64
+def test_geglu_epilogue(I):
     """matmul (ffnIn, N = 2I) followed by geglu: gate = f16(gelu(f16(a)) * f16(b))."""
-    M, I, K, L = 200, 1152, 768, 200
+    M, K, L = 200, 768, 200
     rng = np.random.default_rng(2)
     A = (rng.standard_normal((M, K)) * 0.5).astype(np.float16)
     W = (rng.standard_normal((2 * I, K)) * 0.05).astype(np.float16)
@@ -114,9 +116,10 @@ def test_geglu_epilogue():
     assert_f16_close(got, want.reshape(-1), "geglu")
 
 
-def test_rope_epilogue():
+@pytest.mark.parametrize("H", [12, 6])  # N = 2304 (256-wide tiles) and 1152 (128-wide)
+def test_rope_epilogue(H):
     """matmul (qkv) followed by rope: q and k heads rotated with the table row of the position."""
-    H, D = 12, 64
+    D = 64
     M, N, K, L = 150, 3 * H * D, 768, 150
     rng = np.random.default_rng(3)
     A = (rng.standard_normal((M, K)) * 0.5).astype(np.float16)
