@@ -265,124 +265,145 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
     named_bar(1, 128);
     const uint32_t trow = tmem + (uint32_t(quarter * 32) << 16);
     bool ok = true;
-    for (int hh = 0; hh < HG && ok; ++hh) {
-      float m = -3.40282346638528859812e38f, l = 0.f;
-      float o[D];
+    // Items run in order; the PV product of item it is folded into the context only after the
+    // row maximum of item it + 1 is known, so its latency overlaps that pass. O of the last item
+    // of a head is folded in (and the head's context written) before the next head starts.
+    float m = -3.40282346638528859812e38f, l = 0.f, corr_prev = 1.f;
+    float o[D];
 #pragma unroll
-      for (int d = 0; d < D; ++d) o[d] = 0.f;
-      for (int j = 0; j < nkt; ++j) {
-        const int it = hh * nkt + j;
-        const int k0 = kstart + j * TKEYS;
-        const bool holes = (hbits[j * 4] | hbits[j * 4 + 1] | hbits[j * 4 + 2] | hbits[j * 4 + 3]) != 0;
-        const int clo = min(max(lo - k0, 0), TKEYS), chi = min(max(hi - k0, 0), TKEYS);
-        if (*abort_flag || !mbar_wait(s_full, uint32_t(it & 1), 41)) { ok = false; break; }
-        fence_after_sync();
-        // pass 1: the row maximum of the kept raw scores (four independent chains)
-        float mr[4] = {-3.40282346638528859812e38f, -3.40282346638528859812e38f, -3.40282346638528859812e38f,
-                       -3.40282346638528859812e38f};
+    for (int d = 0; d < D; ++d) o[d] = 0.f;
+    // folds O of item `it` (scaled state: o = o * corr + O) into the context row
+    auto fold = [&](int it, float corr) -> bool {
+      if (*abort_flag || !mbar_wait(o_full, uint32_t(it & 1), 43)) return false;
+      fence_after_sync();
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(trow + 128 + c * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[c * 32 + i] = fmaf(o[c * 32 + i], corr, __uint_as_float(r[i]));
+      }
+      return true;
+    };
+    auto finish_head = [&](int hh) {
+      if (!in_range) return;
+      // a masked query row, or one without a kept key, is exactly zero (select, not multiply)
+      const bool live = qvalid && l > 0.f;
+      const float inv = live ? 1.0f / l : 0.f;
+      uint4* dst = reinterpret_cast<uint4*>(p.ctx + int64_t(row) * H * D + int64_t(hg0 + hh) * D);
+#pragma unroll
+      for (int q = 0; q < D / 8; ++q) {
+        __half2 hv[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          hv[e] = live ? __floats2half2_rn(o[q * 8 + 2 * e] * inv, o[q * 8 + 2 * e + 1] * inv)
+                       : __floats2half2_rn(0.f, 0.f);
+        dst[q] = *reinterpret_cast<uint4*>(hv);
+      }
+    };
+    for (int it = 0; it < NI && ok; ++it) {
+      const int hh = it / nkt, j = it - hh * nkt;
+      const int k0 = kstart + j * TKEYS;
+      const bool holes = (hbits[j * 4] | hbits[j * 4 + 1] | hbits[j * 4 + 2] | hbits[j * 4 + 3]) != 0;
+      const int clo = min(max(lo - k0, 0), TKEYS), chi = min(max(hi - k0, 0), TKEYS);
+      if (*abort_flag || !mbar_wait(s_full, uint32_t(it & 1), 41)) { ok = false; break; }
+      fence_after_sync();
+      // pass 1: the row maximum of the kept raw scores (four independent chains)
+      float mr[4] = {-3.40282346638528859812e38f, -3.40282346638528859812e38f, -3.40282346638528859812e38f,
+                     -3.40282346638528859812e38f};
 #pragma unroll 1
-        for (int c4 = 0; c4 < 4; ++c4) {
-          const bool need = c4 * 32 < chi && c4 * 32 + 32 > clo;
-          if (!__any_sync(0xffffffffu, need)) continue;
+      for (int c4 = 0; c4 < 4; ++c4) {
+        const bool need = c4 * 32 < chi && c4 * 32 + 32 > clo;
+        if (!__any_sync(0xffffffffu, need)) continue;
+        uint32_t r[32];
+        tmem_ld32(trow + c4 * 32, r);
+        tmem_ld_wait();
+        if (!need) continue;
+        if (!holes && clo <= c4 * 32 && c4 * 32 + 32 <= chi) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) mr[i & 3] = fmaxf(mr[i & 3], __uint_as_float(r[i]));
+        } else {
+          const uint32_t vw = holes ? vbits[j * 4 + c4] : 0xffffffffu;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int c = c4 * 32 + i;
+            if (c >= clo && c < chi && ((vw >> i) & 1u)) mr[i & 3] = fmaxf(mr[i & 3], __uint_as_float(r[i]));
+          }
+        }
+      }
+      // the previous item's PV is done by now: fold it in (P and O are free again)
+      if (it > 0) {
+        if (!fold(it - 1, corr_prev)) { ok = false; break; }
+        if (j == 0) {  // a new head: write the previous one and start over
+          finish_head(hh - 1);
+          m = -3.40282346638528859812e38f;
+          l = 0.f;
+#pragma unroll
+          for (int d = 0; d < D; ++d) o[d] = 0.f;
+        }
+      }
+      const float mraw = fmaxf(fmaxf(mr[0], mr[1]), fmaxf(mr[2], mr[3]));
+      const float mx = fmaxf(m, mraw * p.scale_log2);
+      const float corr = ex2_approx(m - mx);
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};
+      // pass 2: p = exp2(s scale log2e - max) in f16, into this row of P (128-byte swizzled)
+#pragma unroll 1
+      for (int c4 = 0; c4 < 4; ++c4) {
+        const bool need = c4 * 32 < chi && c4 * 32 + 32 > clo;
+        uint32_t packed[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) packed[i] = 0u;
+        if (__any_sync(0xffffffffu, need)) {
           uint32_t r[32];
           tmem_ld32(trow + c4 * 32, r);
           tmem_ld_wait();
-          if (!need) continue;
-          if (!holes && clo <= c4 * 32 && c4 * 32 + 32 <= chi) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) mr[i & 3] = fmaxf(mr[i & 3], __uint_as_float(r[i]));
-          } else {
+          if (need) {
+            const bool whole = !holes && clo <= c4 * 32 && c4 * 32 + 32 <= chi;
             const uint32_t vw = holes ? vbits[j * 4 + c4] : 0xffffffffu;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int c = c4 * 32 + i;
-              if (c >= clo && c < chi && ((vw >> i) & 1u)) mr[i & 3] = fmaxf(mr[i & 3], __uint_as_float(r[i]));
-            }
-          }
-        }
-        const float mraw = fmaxf(fmaxf(mr[0], mr[1]), fmaxf(mr[2], mr[3]));
-        const float mx = fmaxf(m, mraw * p.scale_log2);
-        const float corr = ex2_approx(m - mx);
-        float ls[4] = {0.f, 0.f, 0.f, 0.f};
-        // pass 2: p = exp2(s scale log2e - max) in f16, into this row of P (128-byte swizzled)
-#pragma unroll 1
-        for (int c4 = 0; c4 < 4; ++c4) {
-          const bool need = c4 * 32 < chi && c4 * 32 + 32 > clo;
-          uint32_t packed[16];
+            for (int i = 0; i < 32; i += 2) {
+              float pv[2];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) packed[i] = 0u;
-          if (__any_sync(0xffffffffu, need)) {
-            uint32_t r[32];
-            tmem_ld32(trow + c4 * 32, r);
-            tmem_ld_wait();
-            if (need) {
-              const bool whole = !holes && clo <= c4 * 32 && c4 * 32 + 32 <= chi;
-              const uint32_t vw = holes ? vbits[j * 4 + c4] : 0xffffffffu;
-#pragma unroll
-              for (int i = 0; i < 32; i += 2) {
-                float pv[2];
-#pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                  const int c = c4 * 32 + i + e;
-                  const bool keep = whole || (c >= clo && c < chi && ((vw >> (i + e)) & 1u));
-                  pv[e] = keep ? ex2_approx(fmaf(__uint_as_float(r[i + e]), p.scale_log2, -mx)) : 0.f;
-                  ls[(i + e) & 3] += pv[e];
-                }
-                __half2 hv = __floats2half2_rn(pv[0], pv[1]);
-                packed[i / 2] = *reinterpret_cast<uint32_t*>(&hv);
+              for (int e = 0; e < 2; ++e) {
+                const int c = c4 * 32 + i + e;
+                const bool keep = whole || (c >= clo && c < chi && ((vw >> (i + e)) & 1u));
+                pv[e] = keep ? ex2_approx(fmaf(__uint_as_float(r[i + e]), p.scale_log2, -mx)) : 0.f;
+                ls[(i + e) & 3] += pv[e];
               }
+              __half2 hv = __floats2half2_rn(pv[0], pv[1]);
+              packed[i / 2] = *reinterpret_cast<uint32_t*>(&hv);
             }
           }
-          // keys c4*32 .. +31: block c4/2, 16-byte chunks 4 (c4 % 2) .. +3 of this row, swizzled
-          uint8_t* prow = sP + (c4 >> 1) * 16384 + r_local * 128;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int ch = (c4 & 1) * 4 + q;
-            *reinterpret_cast<uint4*>(prow + ((ch ^ (r_local & 7)) * 16)) =
-                make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
-          }
         }
-        l = l * corr + ((ls[0] + ls[1]) + (ls[2] + ls[3]));
-        m = mx;
-        fence_before_sync();
-        mbar_arrive(s_empty);
-        // value rows of masked or absent keys become zero before the PV product
-        const int vs = it % C::VS;
-        if (*abort_flag || !mbar_wait(&v_full[vs], uint32_t(it / C::VS) & 1, 42)) { ok = false; break; }
-        if (!((vbits[j * 4 + sw] >> (st & 31)) & 1u)) {
-          uint4* vrow = reinterpret_cast<uint4*>(sV + vs * C::TILE + st * C::ROW_BYTES);
+        // keys c4*32 .. +31: block c4/2, 16-byte chunks 4 (c4 % 2) .. +3 of this row, swizzled
+        uint8_t* prow = sP + (c4 >> 1) * 16384 + r_local * 128;
 #pragma unroll
-          for (int q = 0; q < C::ROW_BYTES / 16; ++q) vrow[q] = make_uint4(0, 0, 0, 0);
-        }
-        fence_proxy_async_smem();
-        mbar_arrive(p_full);
-        if (*abort_flag || !mbar_wait(o_full, uint32_t(it & 1), 43)) { ok = false; break; }
-        fence_after_sync();
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(trow + 128 + c * 32, r);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[c * 32 + i] = fmaf(o[c * 32 + i], corr, __uint_as_float(r[i]));
+        for (int q = 0; q < 4; ++q) {
+          const int ch = (c4 & 1) * 4 + q;
+          *reinterpret_cast<uint4*>(prow + ((ch ^ (r_local & 7)) * 16)) =
+              make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
         }
       }
-      if (!ok) break;
-      if (in_range) {
-        // a masked query row, or one without a kept key, is exactly zero (select, not multiply)
-        const bool live = qvalid && l > 0.f;
-        const float inv = live ? 1.0f / l : 0.f;
-        uint4* dst = reinterpret_cast<uint4*>(p.ctx + int64_t(row) * H * D + int64_t(hg0 + hh) * D);
+      l = l * corr + ((ls[0] + ls[1]) + (ls[2] + ls[3]));
+      m = mx;
+      corr_prev = corr;
+      fence_before_sync();
+      mbar_arrive(s_empty);
+      // value rows of masked or absent keys become zero before the PV product
+      const int vs = it % C::VS;
+      if (*abort_flag || !mbar_wait(&v_full[vs], uint32_t(it / C::VS) & 1, 42)) { ok = false; break; }
+      if (!((vbits[j * 4 + sw] >> (st & 31)) & 1u)) {
+        uint4* vrow = reinterpret_cast<uint4*>(sV + vs * C::TILE + st * C::ROW_BYTES);
 #pragma unroll
-        for (int q = 0; q < D / 8; ++q) {
-          __half2 hv[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e)
-            hv[e] = live ? __floats2half2_rn(o[q * 8 + 2 * e] * inv, o[q * 8 + 2 * e + 1] * inv)
-                         : __floats2half2_rn(0.f, 0.f);
-          dst[q] = *reinterpret_cast<uint4*>(hv);
-        }
+        for (int q = 0; q < C::ROW_BYTES / 16; ++q) vrow[q] = make_uint4(0, 0, 0, 0);
       }
+      fence_proxy_async_smem();
+      mbar_arrive(p_full);
+    }
+    if (ok && NI > 0) {
+      ok = fold(NI - 1, corr_prev);
+      if (ok) finish_head(HG - 1);
     }
     if (!ok) *abort_flag = 1;
   }

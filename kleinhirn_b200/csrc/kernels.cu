@@ -174,33 +174,43 @@ template <> struct Vec<float> {
 
 constexpr int MAXV = 4;  // vectors per lane: N <= 32 * 4 * 8 (f16) or 32 * 4 * 4 (f32)
 
-// x: the row as nv vectors of Vec<T>::N values, v[k] holds vector lane + 32 k.
-template <typename T>
+// Groups of LPR lanes (8, 16 or 32) own one row each: lane i of a group holds vectors
+// i, i + LPR, ... (v[k] = vector i + LPR k) and the reductions stay inside the group.
+template <int LPR>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+  for (int o = LPR / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <typename T, int LPR>
 __device__ __forceinline__ void ln_vec_finish(float (&v)[MAXV][8], int N, const T* __restrict__ w,
-                                              const T* __restrict__ bias, float eps, float scale, T* __restrict__ out) {
+                                              const T* __restrict__ bias, float eps, float scale, T* __restrict__ out,
+                                              bool live) {
   constexpr int VN = Vec<T>::N;
-  const int lane = threadIdx.x & 31;
+  const int gl = threadIdx.x & (LPR - 1);
   const int nv = N / VN;
   float s = 0.f;
 #pragma unroll
   for (int k = 0; k < MAXV; ++k)
-    if (lane + 32 * k < nv)
+    if (gl + LPR * k < nv)
 #pragma unroll
       for (int e = 0; e < VN; ++e) s += v[k][e];
-  const float mean = warp_sum(s) / float(N);
+  const float mean = group_sum<LPR>(s) / float(N);
   float q = 0.f;
 #pragma unroll
   for (int k = 0; k < MAXV; ++k)
-    if (lane + 32 * k < nv)
+    if (gl + LPR * k < nv)
 #pragma unroll
       for (int e = 0; e < VN; ++e) {
         const float x = v[k][e] - mean;
         q += x * x;
       }
-  const float inv = 1.0f / sqrtf(warp_sum(q) / float(N) + eps);
+  const float inv = 1.0f / sqrtf(group_sum<LPR>(q) / float(N) + eps);
+  if (!live) return;
 #pragma unroll
   for (int k = 0; k < MAXV; ++k) {
-    const int idx = lane + 32 * k;
+    const int idx = gl + LPR * k;
     if (idx < nv) {
       float wv[8], bv[8], y[8];
       Vec<T>::load(w + idx * VN, wv);
@@ -212,20 +222,20 @@ __device__ __forceinline__ void ln_vec_finish(float (&v)[MAXV][8], int N, const 
   }
 }
 
-template <typename T>
+template <typename T, int LPR>
 __global__ void layernorm_vec_kernel(const T* __restrict__ a, const T* __restrict__ bb, const T* __restrict__ w,
                                      const T* __restrict__ bias, const float* __restrict__ mask, T* __restrict__ out,
                                      int N, int rows, int mode, float eps) {
   constexpr int VN = Vec<T>::N;
-  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (row >= rows) return;
-  const int lane = threadIdx.x & 31;
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) / LPR;
+  const bool live = row < rows;  // every lane of a warp takes part in the shuffles
+  const int gl = threadIdx.x & (LPR - 1);
   const int nv = N / VN;
-  const int64_t base = int64_t(row) * N;
+  const int64_t base = int64_t(live ? row : 0) * N;
   float v[MAXV][8];
 #pragma unroll
   for (int k = 0; k < MAXV; ++k) {
-    const int idx = lane + 32 * k;
+    const int idx = gl + LPR * k;
     if (idx < nv) {
       Vec<T>::load(a + base + idx * VN, v[k]);
       if (mode == 2) {
@@ -236,19 +246,20 @@ __global__ void layernorm_vec_kernel(const T* __restrict__ a, const T* __restric
       }
     }
   }
-  ln_vec_finish<T>(v, N, w, bias, eps, mode == 1 ? mask[row] : 1.0f, out + base);
+  ln_vec_finish<T, LPR>(v, N, w, bias, eps, (mode == 1 && live) ? mask[row] : 1.0f, out + base, live);
 }
 
-template <typename T>
+template <typename T, int LPR>
 __global__ void embln_vec_kernel(const T* __restrict__ word, const T* __restrict__ pos, const T* __restrict__ typ,
                                  const uint32_t* __restrict__ tt, const T* __restrict__ w, const T* __restrict__ b,
                                  const float* __restrict__ mask, T* __restrict__ out, int N, int rows,
                                  const int32_t* __restrict__ row_pos, int offset, int maxpos, float eps, int maskmul,
                                  int posids) {
   constexpr int VN = Vec<T>::N;
-  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (row >= rows) return;
-  const int lane = threadIdx.x & 31;
+  const int row0 = (blockIdx.x * blockDim.x + threadIdx.x) / LPR;
+  const bool live = row0 < rows;
+  const int row = live ? row0 : 0;
+  const int gl = threadIdx.x & (LPR - 1);
   const uint32_t t = tt ? tt[row] : 0u;
   int prow = posids ? int(t >> 16) : row_pos[row] + offset;
   prow = min(prow, maxpos - 1);
@@ -257,7 +268,7 @@ __global__ void embln_vec_kernel(const T* __restrict__ word, const T* __restrict
   float v[MAXV][8];
 #pragma unroll
   for (int k = 0; k < MAXV; ++k) {
-    const int idx = lane + 32 * k;
+    const int idx = gl + LPR * k;
     if (idx < nv) {
       float x[8], y[8], z[8];
       Vec<T>::load(word + wbase + idx * VN, x);
@@ -267,8 +278,11 @@ __global__ void embln_vec_kernel(const T* __restrict__ word, const T* __restrict
       for (int e = 0; e < VN; ++e) v[k][e] = x[e] + y[e] + z[e];
     }
   }
-  ln_vec_finish<T>(v, N, w, b, eps, maskmul ? mask[row] : 1.0f, out + wbase);
+  ln_vec_finish<T, LPR>(v, N, w, b, eps, (maskmul && live) ? mask[row] : 1.0f, out + wbase, live);
 }
+
+// Lanes per row of the vectorised row kernels: the fewest with at most MAXV vectors each.
+inline int lanes_per_row(int nv) { return nv <= 8 * MAXV ? 8 : nv <= 16 * MAXV ? 16 : 32; }
 
 template <typename T>
 __global__ void add_kernel(T* __restrict__ dst, const T* __restrict__ src, int64_t count) {
@@ -530,15 +544,18 @@ void launch_embln(bool f16, const void* word, const void* pos, const void* typ, 
   if (rows <= 0) return;
   const int vn = f16 ? 8 : 4;
   if (N % vn == 0 && N / vn <= 32 * MAXV) {
-    const int g4 = (rows + 3) / 4;
-    if (f16)
-      embln_vec_kernel<__half><<<g4, 128, 0, st>>>((const __half*)word, (const __half*)pos, (const __half*)typ, tt,
-                                                   (const __half*)w, (const __half*)b, mask, (__half*)out, N, rows,
-                                                   row_pos, offset, maxpos, eps, maskmul, posids);
-    else
-      embln_vec_kernel<float><<<g4, 128, 0, st>>>((const float*)word, (const float*)pos, (const float*)typ, tt,
-                                                  (const float*)w, (const float*)b, mask, (float*)out, N, rows,
-                                                  row_pos, offset, maxpos, eps, maskmul, posids);
+    const int lpr = lanes_per_row(N / vn);
+    const int grid = int((int64_t(rows) * lpr + 255) / 256);
+#define KH_EMBLN(TT, L)                                                                                         \
+  embln_vec_kernel<TT, L><<<grid, 256, 0, st>>>((const TT*)word, (const TT*)pos, (const TT*)typ, tt, (const TT*)w, \
+                                                (const TT*)b, mask, (TT*)out, N, rows, row_pos, offset, maxpos, eps, \
+                                                maskmul, posids)
+    if (f16) {
+      if (lpr == 8) KH_EMBLN(__half, 8); else if (lpr == 16) KH_EMBLN(__half, 16); else KH_EMBLN(__half, 32);
+    } else {
+      if (lpr == 8) KH_EMBLN(float, 8); else if (lpr == 16) KH_EMBLN(float, 16); else KH_EMBLN(float, 32);
+    }
+#undef KH_EMBLN
     return;
   }
   const int grid = (rows + 7) / 8;
@@ -558,13 +575,17 @@ void launch_layernorm(bool f16, const void* a, const void* b, const void* w, con
   if (rows <= 0) return;
   const int vn = f16 ? 8 : 4;
   if (N % vn == 0 && N / vn <= 32 * MAXV) {
-    const int g4 = (rows + 3) / 4;
-    if (f16)
-      layernorm_vec_kernel<__half><<<g4, 128, 0, st>>>((const __half*)a, (const __half*)b, (const __half*)w,
-                                                       (const __half*)bias, mask, (__half*)out, N, rows, mode, eps);
-    else
-      layernorm_vec_kernel<float><<<g4, 128, 0, st>>>((const float*)a, (const float*)b, (const float*)w,
-                                                      (const float*)bias, mask, (float*)out, N, rows, mode, eps);
+    const int lpr = lanes_per_row(N / vn);
+    const int grid = int((int64_t(rows) * lpr + 255) / 256);
+#define KH_LN(TT, L)                                                                                            \
+  layernorm_vec_kernel<TT, L><<<grid, 256, 0, st>>>((const TT*)a, (const TT*)b, (const TT*)w, (const TT*)bias, mask, \
+                                                    (TT*)out, N, rows, mode, eps)
+    if (f16) {
+      if (lpr == 8) KH_LN(__half, 8); else if (lpr == 16) KH_LN(__half, 16); else KH_LN(__half, 32);
+    } else {
+      if (lpr == 8) KH_LN(float, 8); else if (lpr == 16) KH_LN(float, 16); else KH_LN(float, 32);
+    }
+#undef KH_LN
     return;
   }
   const int grid = (rows + 7) / 8;
