@@ -2,20 +2,25 @@
 // (the activations), W [N, K] f16 row-major (PyTorch [out, in] weights, as the reference stores
 // them, src/convert/names.ts:5), f32 accumulation in TMEM.
 //
-// Tiles are 128 x BN with BN = 256 when N is a multiple of 256 (the operands of one N = 256 MMA
-// step stay within the shared-memory bandwidth of the SM), else BN = 128.
-// One persistent CTA per SM, 320 threads in three roles:
-//   warp 0      TMA producer: 128 x 64 tiles of A and BN x 64 tiles of W into a ring of STAGES
-//               shared-memory stages (128-byte swizzle), completion on per-stage mbarriers;
-//   warp 1      MMA issuer: one thread issues tcgen05.mma kind::f16 (M 128, N BN, K 16) into
-//               one of two TMEM accumulators, commits each stage back to the producer and each
-//               finished tile to the epilogue;
-//   warps 2-9   epilogue, two warpgroups: warpgroup g takes accumulator columns
-//               [g BN / 2, (g + 1) BN / 2) (warp w reads TMEM lanes 32 (w % 4) ..); bias, activation and the fused
-//               follow-up op in registers, the f16 result into a swizzled shared-memory tile,
-//               written out by one TMA store per warpgroup (rows and columns past M and N are
-//               clipped by the tensor map).
-// Tiles run n-fastest so the CTAs working at the same time share rows of A in L2.
+// Tiles are 256 x BN, computed by a cluster of two CTAs on two SMs (tcgen05 cta_group::2), with
+// BN = 256 when N is a multiple of 256, else 192 when N is a multiple of 192, else 128. Each CTA
+// stages its own 128 rows of A and BN / 2 rows of W; one thread of the first CTA issues the
+// M = 256 MMAs, which read both CTAs' shared memory, and each CTA's TMEM holds its 128 rows of
+// the accumulator. Per SM and K = 16 step the MMAs then read 4 KB of A and BN / 32 KB of W from
+// shared memory (with one-SM 128 x BN tiles: 4 + BN / 16 KB), which together with the TMA writes
+// stays within the SM's shared-memory bandwidth.
+// Persistent: one cluster per SM pair, 64 + 128 BN / 64 threads per CTA in three roles:
+//   warp 0      TMA producer (both CTAs): 128 x 64 tiles of A and BN / 2 x 64 tiles of W into a
+//               ring of STAGES shared-memory stages (128-byte swizzle); both CTAs' bytes complete
+//               on the first CTA's stage barrier;
+//   warp 1      MMA issuer (first CTA): tcgen05.mma kind::f16 (M 256, N BN, K 16) into one of two
+//               TMEM accumulators; each stage is committed back to both CTAs' producers and each
+//               finished tile to both CTAs' epilogues;
+//   warps 2..   epilogue, one warpgroup per 64 accumulator columns (warp w reads TMEM lanes
+//               32 (w % 4) ..): bias, activation and the fused follow-up op in registers, the f16
+//               result into a swizzled shared-memory tile, written out by one TMA store per
+//               warpgroup (rows and columns past M and N are clipped by the tensor map).
+// Tiles run n-fastest so the pairs working at the same time share rows of A in L2.
 //
 // Epilogues reproduce the reference's storage rounding exactly (every value the reference
 // stores in the plan's f16 buffer is rounded to f16 here before it is used again):
@@ -45,27 +50,24 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int A_BYTES = BM * BK * 2;
 constexpr int OUT_BYTES = 128 * 64 * 2;  // one warpgroup's staged output tile
-constexpr int THREADS = 320;
-constexpr int EPI_THREADS = 256;
 
 template <int BN>
 struct GCfg {
   static constexpr int STAGES = BN == 256 ? 3 : 4;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr uint32_t TMEM_COLS = 2 * BN;
-  static constexpr int SMEM = STAGES * (A_BYTES + B_BYTES) + 4 * OUT_BYTES + 1024 + 256;
-  static constexpr int WG_COLS = BN / 2;  // accumulator columns of one epilogue warpgroup
+  static constexpr int NWG = BN / 64;                // epilogue warpgroups, 64 columns each
+  static constexpr int THREADS = 64 + 128 * NWG;     // producer warp, MMA warp, epilogue
+  static constexpr int SBUF = BN == 256 ? 1 : 2;     // staging tiles per warpgroup
+  static constexpr int SMEM = STAGES * (A_BYTES + B_BYTES) + NWG * SBUF * OUT_BYTES + 1024 + 256;
 };
 
-enum Epi { EPI_PLAIN = 0, EPI_RESIDUAL = 1, EPI_GEGLU = 2, EPI_ROPE = 3 };
+// Epilogue modes (compile time): 0-4 plain with activation ACT, then the fused follow-up ops.
+enum EpiMode { EPI_MODE_RESIDUAL = 5, EPI_MODE_GEGLU = 6, EPI_MODE_ROPE = 7 };
 
 struct Params {
   int M, N, K;
   const __half* bias;
-  const __half* C;  // residual source (the output itself)
-  int ldc;
-  int act;
-  int epi;
   const float* table;
   const int32_t* row_pos;
   int rope_cols;  // columns of q and k (2 H D), heads of 64
@@ -109,15 +111,6 @@ __device__ __forceinline__ void load32h(const __half* src, float (&v)[32]) {
   }
 }
 
-__device__ __forceinline__ void bias32(const __half* b, int n, float (&v)[32]) {
-  if (b) {
-    load32h(b + n, v);
-  } else {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = 0.f;
-  }
-}
-
 // Row r of a staged tile with 128-byte rows (128-byte swizzle, the TMA layout of a 64-column
 // f16 box): the 16-byte chunks ch .. ch + 3 hold v[0 .. 31].
 __device__ __forceinline__ void stage32_sw128(uint8_t* tile, int r, int ch, const float (&v)[32]) {
@@ -143,22 +136,48 @@ __device__ __forceinline__ void stage32_sw64(uint8_t* tile, int r, const float (
   }
 }
 
-template <int BN>
-__global__ void __launch_bounds__(THREADS, 1)
+// Bias and activation of 32 accumulator columns [n, n + 32) of one row, in place.
+template <int MODE>
+__device__ __forceinline__ void bias_act32(float (&v)[32], const __half* bias, int n) {
+  if (bias) {
+    const uint4* s = reinterpret_cast<const uint4*>(bias + n);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 u = __ldg(s + q);
+      const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __half22float2(h[e]);
+        v[q * 8 + 2 * e] += f.x;
+        v[q * 8 + 2 * e + 1] += f.y;
+      }
+    }
+  }
+  if constexpr (MODE >= 1 && MODE <= 4) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = act_fn(v[i], MODE);
+  }
+}
+
+template <int BN, int MODE>
+__global__ void __launch_bounds__(GCfg<BN>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const Params p) {
   using G = GCfg<BN>;
   constexpr int STAGES = G::STAGES;
+  constexpr int NWG = G::NWG;
+  constexpr int SBUF = G::SBUF;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint8_t* sOut = sB + STAGES * G::B_BYTES;  // [warpgroup][2] 16 KB staging tiles
-  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + 4 * OUT_BYTES);
+  uint8_t* sOut = sB + STAGES * G::B_BYTES;  // [warpgroup][SBUF] 16 KB staging tiles
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + NWG * SBUF * OUT_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
-  uint64_t* drain = tempty + 2;
+  uint64_t* res_full = tempty + 2;  // [warpgroup]: residual tile landed in the staging tile
+  uint64_t* drain = res_full + NWG;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -174,8 +193,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], EPI_THREADS);
+      mbar_init(&tempty[b], 128 * NWG);
     }
+    for (int g = 0; g < NWG; ++g) mbar_init(&res_full[g], 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -263,124 +283,145 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
   } else {
+    // epilogue warpgroup g owns accumulator columns [64 g, 64 g + 64) of every tile
     const int q = warp & 3;          // TMEM lane quarter of this warp
     const int g = (warp - 2) >> 2;   // warpgroup
     const int r = q * 32 + lane;     // row of the tile
     const bool leader = (warp == 2 + 4 * g) && lane == 0;
+    bool res_pending = false;        // a residual load of the leader not yet waited for
+    uint32_t res_loads = 0;          // residual loads of this warpgroup so far (barrier parity)
     int local = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
       const int buf = local & 1;
       const uint32_t tphase = (local >> 1) & 1;
-      if (*abort_flag || !mbar_wait(&tfull[buf], tphase, 4)) {
-        *abort_flag = 1;
-        break;
-      }
-      fence_after_sync();
       const int mb = t / n_tiles, nb = t % n_tiles;
       const int row = mb * BM + r;
       const bool live = row < p.M;
       const int n0 = nb * BN;
-      const uint32_t taddr = tmem + (uint32_t(q * 32) << 16) + uint32_t(buf * BN);
-      if (p.epi == EPI_GEGLU) {
-        // accumulator columns [0, BN/2) hold a, [BN/2, BN) hold b for the tile's BN/2 outputs;
-        // this warpgroup writes outputs [g OC, g OC + OC) of the tile
-        constexpr int OC = BN / 4;
-        uint8_t* stile = sOut + (g * 2 + buf) * OUT_BYTES;
-        if (leader) bulk_wait_read<1>();
-        named_bar(1 + g, 128);
-#pragma unroll 1
-        for (int pc = 0; pc < OC / 32; ++pc) {
-          uint32_t ra[32], rb[32];
-          tmem_ld32(taddr + g * OC + pc * 32, ra);
-          tmem_ld32(taddr + BN / 2 + g * OC + pc * 32, rb);
-          tmem_ld_wait();
-          if (pc == OC / 32 - 1) {
-            fence_before_sync();
-            mbar_arrive(&tempty[buf]);  // the accumulator is read: the MMA may reuse it
-          }
-          float ba[32], bb[32], v[32];
-          bias32(p.bias, n0 + g * OC + pc * 32, ba);
-          bias32(p.bias, n0 + BN / 2 + g * OC + pc * 32, bb);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float a = f16r(__uint_as_float(ra[i]) + ba[i]);
-            const float b = f16r(__uint_as_float(rb[i]) + bb[i]);
-            v[i] = gelu_as(a) * b;
-          }
-          if (OC == 32) stage32_sw64(stile, r, v);
-          else stage32_sw128(stile, r, pc * 4, v);
+      uint8_t* stile = sOut + (g * SBUF + (local % SBUF)) * OUT_BYTES;
+      const int nc = n0 + g * 64;  // first output column of this warpgroup (plain, residual, rope)
+      // the TMA store that last read this staging tile must be done with it
+      if (leader) {
+        bulk_wait_read<SBUF - 1>();
+        if (MODE == EPI_MODE_RESIDUAL && nc < p.N) {
+          // the residual rows of the tile come in by TMA, into the staging tile
+          mbar_arrive_expect_tx(&res_full[g], OUT_BYTES);
+          tma_load_2d(stile, &tmC, &res_full[g], nc, mb * BM);
+          res_pending = true;
         }
+      }
+      const bool failed = *abort_flag || !mbar_wait(&tfull[buf], tphase, 4);
+      // the warpgroup leaves together, so no thread is left waiting at its named barriers
+      if (named_bar_any(1 + g, 128, failed)) {
+        *abort_flag = 1;
+        break;
+      }
+      fence_after_sync();
+      const uint32_t taddr = tmem + (uint32_t(q * 32) << 16) + uint32_t(buf * BN);
+      if constexpr (MODE == EPI_MODE_GEGLU) {
+        // accumulator columns [0, BN/2) hold a, [BN/2, BN) hold b for the tile's BN/2 outputs;
+        // this warpgroup writes outputs [32 g, 32 g + 32) of the tile
+        uint32_t ra[32], rb[32];
+        tmem_ld32(taddr + g * 32, ra);
+        tmem_ld32(taddr + BN / 2 + g * 32, rb);
+        tmem_ld_wait();
+        fence_before_sync();
+        mbar_arrive(&tempty[buf]);  // the accumulator is read: the MMA may reuse it
+        named_bar(1 + g, 128);      // the staging tile is free
+        float a[32], b[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          a[i] = __uint_as_float(ra[i]);
+          b[i] = __uint_as_float(rb[i]);
+        }
+        bias_act32<0>(a, p.bias, n0 + g * 32);
+        bias_act32<0>(b, p.bias, n0 + BN / 2 + g * 32);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) a[i] = gelu_as(f16r(a[i])) * f16r(b[i]);
+        stage32_sw64(stile, r, a);
         fence_proxy_async_smem();
         named_bar(1 + g, 128);
         if (leader) {
-          tma_store_2d(&tmC, stile, nb * (BN / 2) + g * OC, mb * BM);
+          tma_store_2d(&tmC, stile, nb * (BN / 2) + g * 32, mb * BM);
           bulk_commit();
         }
       } else {
-#pragma unroll 1
-        for (int ch = 0; ch < G::WG_COLS / 64; ++ch) {
-          const int nc = n0 + g * G::WG_COLS + ch * 64;
-          uint8_t* stile = sOut + (g * 2 + (BN == 128 ? buf : ch)) * OUT_BYTES;
-          uint32_t r0[32], r1[32];
-          tmem_ld32(taddr + g * G::WG_COLS + ch * 64, r0);
-          tmem_ld32(taddr + g * G::WG_COLS + ch * 64 + 32, r1);
-          tmem_ld_wait();
-          if (ch == G::WG_COLS / 64 - 1) {
-            fence_before_sync();
-            mbar_arrive(&tempty[buf]);  // the accumulator is read: the MMA may reuse it
-          }
-          // the TMA store that last read this staging tile must be done with it
-          if (leader) bulk_wait_read<1>();
-          named_bar(1 + g, 128);
-          float v0[32], v1[32];
-          bias32(p.bias, min(nc, p.N - 32), v0);
-          bias32(p.bias, min(nc + 32, p.N - 32), v1);
+        uint32_t r0[32], r1[32];
+        tmem_ld32(taddr + g * 64, r0);
+        tmem_ld32(taddr + g * 64 + 32, r1);
+        tmem_ld_wait();
+        fence_before_sync();
+        mbar_arrive(&tempty[buf]);  // the accumulator is read: the MMA may reuse it
+        float v0[32], v1[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            v0[i] += __uint_as_float(r0[i]);
-            v1[i] += __uint_as_float(r1[i]);
-          }
-          if (p.epi == EPI_ROPE && nc < p.rope_cols) {
+        for (int i = 0; i < 32; ++i) {
+          v0[i] = __uint_as_float(r0[i]);
+          v1[i] = __uint_as_float(r1[i]);
+        }
+        const int nb0 = min(nc, p.N - 64);  // bias columns stay inside N (N % 64 == 0)
+        if constexpr (MODE == EPI_MODE_ROPE) {
+          bias_act32<0>(v0, p.bias, nb0);
+          bias_act32<0>(v1, p.bias, nb0 + 32);
+          if (nc < p.rope_cols) {
             // one 64-wide head: rotate-half with the table row of the local position
-            const float* tb = p.table + int64_t(live ? p.row_pos[row] : 0) * 128;
+            const float4* tb = reinterpret_cast<const float4*>(p.table + int64_t(live ? p.row_pos[row] : 0) * 128);
 #pragma unroll
-            for (int d = 0; d < 32; ++d) {
-              const float x = f16r(v0[d]), y = f16r(v1[d]);
-              const float cs = tb[d], sn = tb[64 + d];
-              v0[d] = x * cs - y * sn;
-              v1[d] = y * cs + x * sn;
-            }
-          } else if (p.epi == EPI_RESIDUAL) {
-            float res[32];
-            if (live && nc < p.N) {
-              load32h(p.C + int64_t(row) * p.ldc + nc, res);
+            for (int d4 = 0; d4 < 8; ++d4) {
+              const float4 c4 = __ldg(tb + d4), s4 = __ldg(tb + 16 + d4);
+              const float cs[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
-              for (int i = 0; i < 32; ++i) v0[i] = res[i] + f16r(v0[i]);
-            }
-            if (live && nc + 32 < p.N) {
-              load32h(p.C + int64_t(row) * p.ldc + nc + 32, res);
-#pragma unroll
-              for (int i = 0; i < 32; ++i) v1[i] = res[i] + f16r(v1[i]);
-            }
-          } else if (p.act) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              v0[i] = act_fn(v0[i], p.act);
-              v1[i] = act_fn(v1[i], p.act);
+              for (int e = 0; e < 4; ++e) {
+                const int d = d4 * 4 + e;
+                const float x = f16r(v0[d]), y = f16r(v1[d]);
+                v0[d] = x * cs[e] - y * sn[e];
+                v1[d] = y * cs[e] + x * sn[e];
+              }
             }
           }
-          stage32_sw128(stile, r, 0, v0);
-          stage32_sw128(stile, r, 4, v1);
-          fence_proxy_async_smem();
-          named_bar(1 + g, 128);
-          if (leader) {
-            if (nc < p.N) tma_store_2d(&tmC, stile, nc, mb * BM);
-            bulk_commit();
+          named_bar(1 + g, 128);  // the staging tile is free
+        } else if constexpr (MODE == EPI_MODE_RESIDUAL) {
+          bias_act32<0>(v0, p.bias, nb0);
+          bias_act32<0>(v1, p.bias, nb0 + 32);
+          if (nc < p.N) {  // every thread sees the residual tile land
+            if (!mbar_wait(&res_full[g], res_loads & 1u, 5)) *abort_flag = 1;
+            ++res_loads;
+            res_pending = false;
           }
+          // residual row r of the staged tile (128-byte swizzle): C + f16(acc + bias)
+          const uint8_t* srow = stile + r * 128;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const uint4 u = *reinterpret_cast<const uint4*>(srow + ((c ^ (r & 7)) * 16));
+            const __half2* h = reinterpret_cast<const __half2*>(&u);
+            float* v = c < 4 ? v0 : v1;
+            const int o = (c & 3) * 8;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = __half22float2(h[e]);
+              v[o + 2 * e] = f.x + f16r(v[o + 2 * e]);
+              v[o + 2 * e + 1] = f.y + f16r(v[o + 2 * e + 1]);
+            }
+          }
+        } else {
+          bias_act32<MODE>(v0, p.bias, nb0);
+          bias_act32<MODE>(v1, p.bias, nb0 + 32);
+          named_bar(1 + g, 128);  // the staging tile is free
+        }
+        stage32_sw128(stile, r, 0, v0);
+        stage32_sw128(stile, r, 4, v1);
+        fence_proxy_async_smem();
+        named_bar(1 + g, 128);
+        if (leader) {
+          if (nc < p.N) tma_store_2d(&tmC, stile, nc, mb * BM);
+          bulk_commit();
         }
       }
     }
-    if (leader) bulk_wait<0>();
+    if (leader) {
+      // a residual load issued for a tile the loop left early must land before the CTA ends
+      if (res_pending) mbar_wait(&res_full[g], res_loads & 1u, 13);
+      bulk_wait<0>();
+    }
   }
   fence_before_sync();
   __syncthreads();
@@ -390,14 +431,312 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
+// ---- CTA pairs: 256 x BN tiles on two SMs (cta_group::2) ----
+//
+// A cluster of two CTAs computes a 256 x BN tile with one MMA stream: each CTA stages its own
+// 128 rows of A and its own BN/2 rows of W, one thread of the first CTA issues M = 256 MMAs
+// that read both CTAs' shared memory, and each CTA's TMEM receives its 128 rows of the
+// accumulator. Per SM, one K = 16 step reads 4 KB of A and BN/32 KB of W from shared memory
+// instead of 4 + BN/16 KB, which keeps the operand traffic of the MMAs and the TMA writes within
+// the SM's shared-memory bandwidth.
+template <int BN>
+struct PCfg {
+  static constexpr int BH = BN / 2;  // W rows staged per CTA
+  static constexpr int B_BYTES = BH * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int NWG = BN / 64;
+  static constexpr int THREADS = 64 + 128 * NWG;
+  static constexpr int SBUF = BN == 128 ? 2 : 1;
+  static constexpr int STAGES = BN == 256 ? 4 : (BN == 192 ? 5 : 6);
+  static constexpr uint32_t TMEM_COLS = BN == 128 ? 256 : 512;
+  static constexpr int ACC_STRIDE = BN == 128 ? 128 : 256;  // TMEM columns between the two accumulators
+  static constexpr int SMEM = STAGES * STAGE_BYTES + NWG * SBUF * OUT_BYTES + 1024 + 256;
+};
+
+template <int BN, int MODE>
+__global__ void __launch_bounds__(PCfg<BN>::THREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmC, const Params p) {
+  using G = PCfg<BN>;
+  constexpr int STAGES = G::STAGES;
+  constexpr int NWG = G::NWG;
+  constexpr int SBUF = G::SBUF;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint8_t* sOut = sB + STAGES * G::B_BYTES;  // [warpgroup][SBUF] 16 KB staging tiles
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + NWG * SBUF * OUT_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* res_full = tempty + 2;
+  uint64_t* drain = res_full + NWG;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool first = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int m_tiles = (p.M + 2 * BM - 1) / (2 * BM), n_tiles = (p.N + BN - 1) / BN;
+  const int tiles = m_tiles * n_tiles;
+  const int nk = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 2 * 4 * NWG);  // one arrival per epilogue warp of both CTAs
+    }
+    for (int g = 0; g < NWG; ++g) mbar_init(&res_full[g], 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+    prefetch_tmap(&tmC);
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_holder, G::TMEM_COLS);
+  fence_before_sync();
+  cluster_sync();  // both CTAs' barriers exist before either signals the other
+  fence_after_sync();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0, last_parity = 0;
+      bool ok = true;
+      for (int t = pair; t < tiles && ok; t += npairs) {
+        const int mb = t / n_tiles, nb = t % n_tiles;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (*abort_flag || !mbar_wait(&empty[stage], phase ^ 1, 1)) {
+            ok = false;
+            break;
+          }
+          // both CTAs' bytes of the stage complete on the first CTA's barrier
+          if (first) mbar_arrive_expect_tx(&full[stage], 2 * G::STAGE_BYTES);
+          const uint32_t bar = cluster_addr(&full[stage], 0);
+          tma_load_2d_pair(sA + stage * A_BYTES, &tmA, bar, kb * BK, mb * 2 * BM + int(rank) * BM);
+          tma_load_2d_pair(sB + stage * G::B_BYTES, &tmB, bar, kb * BK, nb * BN + int(rank) * G::BH);
+          issued |= 1u << stage;
+          last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        // the first CTA's barriers count both CTAs' copies: wait for the ones issued
+        if (first)
+          for (int s = 0; s < STAGES; ++s)
+            if (issued & (1u << s)) mbar_wait(&full[s], (last_parity >> s) & 1u, 11);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && first) {
+      const uint32_t idesc = idesc_f16(2 * BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = pair; t < tiles && ok; t += npairs, ++local) {
+        const int buf = local & 1;
+        const uint32_t tphase = (local >> 1) & 1;
+        if (*abort_flag || !mbar_wait(&tempty[buf], tphase ^ 1, 2)) {
+          ok = false;
+          break;
+        }
+        fence_after_sync();
+        const uint32_t d = tmem + uint32_t(buf * G::ACC_STRIDE);
+        for (int kb = 0; kb < nk; ++kb) {
+          if (*abort_flag || !mbar_wait(&full[stage], phase, 3)) {
+            ok = false;
+            break;
+          }
+          fence_after_sync();
+          const uint64_t da = desc_sw128(sA + stage * A_BYTES);
+          const uint64_t db = desc_sw128(sB + stage * G::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            mma_f16_pair(d, da + uint64_t(k * 2), db + uint64_t(k * 2), idesc, (kb | k) != 0 ? 1u : 0u);
+          mma_commit_pair_both(&empty[stage]);  // the stage is free again in both CTAs
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit_pair_both(&tfull[buf]);
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        mma_commit_pair(drain);  // the MMAs in flight finish before the TMEM is freed
+        mbar_wait(drain, 0, 12);
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int g = (warp - 2) >> 2;
+    const int r = q * 32 + lane;
+    const bool leader = (warp == 2 + 4 * g) && lane == 0;
+    bool res_pending = false;
+    uint32_t res_loads = 0;
+    int local = 0;
+    for (int t = pair; t < tiles; t += npairs, ++local) {
+      const int buf = local & 1;
+      const uint32_t tphase = (local >> 1) & 1;
+      const int mb = t / n_tiles, nb = t % n_tiles;
+      const int row0 = mb * 2 * BM + int(rank) * BM;  // first row of this CTA's half of the tile
+      const int row = row0 + r;
+      const bool live = row < p.M;
+      const int n0 = nb * BN;
+      uint8_t* stile = sOut + (g * SBUF + (local % SBUF)) * OUT_BYTES;
+      const int nc = n0 + g * 64;
+      if (leader) {
+        bulk_wait_read<SBUF - 1>();
+        if (MODE == EPI_MODE_RESIDUAL && nc < p.N) {
+          mbar_arrive_expect_tx(&res_full[g], OUT_BYTES);
+          tma_load_2d(stile, &tmC, &res_full[g], nc, row0);
+          res_pending = true;
+        }
+      }
+      const bool failed = *abort_flag || !mbar_wait(&tfull[buf], tphase, 4);
+      if (named_bar_any(1 + g, 128, failed)) {
+        *abort_flag = 1;
+        break;
+      }
+      fence_after_sync();
+      const uint32_t taddr = tmem + (uint32_t(q * 32) << 16) + uint32_t(buf * G::ACC_STRIDE);
+      // tells the MMA thread that this warp has read its accumulator rows
+      auto release_acc = [&]() {
+        fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(cluster_addr(&tempty[buf], 0));
+      };
+      if constexpr (MODE == EPI_MODE_GEGLU) {
+        constexpr int OC = BN / 2 / NWG;  // outputs of one warpgroup: 32
+        static_assert(OC == 32, "geglu warpgroups write 32 outputs");
+        uint32_t ra[32], rb[32];
+        tmem_ld32(taddr + g * 32, ra);
+        tmem_ld32(taddr + BN / 2 + g * 32, rb);
+        tmem_ld_wait();
+        release_acc();
+        named_bar(1 + g, 128);
+        float a[32], b[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          a[i] = __uint_as_float(ra[i]);
+          b[i] = __uint_as_float(rb[i]);
+        }
+        bias_act32<0>(a, p.bias, n0 + g * 32);
+        bias_act32<0>(b, p.bias, n0 + BN / 2 + g * 32);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) a[i] = gelu_as(f16r(a[i])) * f16r(b[i]);
+        stage32_sw64(stile, r, a);
+        fence_proxy_async_smem();
+        named_bar(1 + g, 128);
+        if (leader) {
+          tma_store_2d(&tmC, stile, nb * (BN / 2) + g * 32, row0);
+          bulk_commit();
+        }
+      } else {
+        uint32_t r0[32], r1[32];
+        tmem_ld32(taddr + g * 64, r0);
+        tmem_ld32(taddr + g * 64 + 32, r1);
+        tmem_ld_wait();
+        release_acc();
+        float v0[32], v1[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          v0[i] = __uint_as_float(r0[i]);
+          v1[i] = __uint_as_float(r1[i]);
+        }
+        const int nb0 = min(nc, p.N - 64);
+        if constexpr (MODE == EPI_MODE_ROPE) {
+          bias_act32<0>(v0, p.bias, nb0);
+          bias_act32<0>(v1, p.bias, nb0 + 32);
+          if (nc < p.rope_cols) {
+            const float4* tb = reinterpret_cast<const float4*>(p.table + int64_t(live ? p.row_pos[row] : 0) * 128);
+#pragma unroll
+            for (int d4 = 0; d4 < 8; ++d4) {
+              const float4 c4 = __ldg(tb + d4), s4 = __ldg(tb + 16 + d4);
+              const float cs[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int d = d4 * 4 + e;
+                const float x = f16r(v0[d]), y = f16r(v1[d]);
+                v0[d] = x * cs[e] - y * sn[e];
+                v1[d] = y * cs[e] + x * sn[e];
+              }
+            }
+          }
+          named_bar(1 + g, 128);
+        } else if constexpr (MODE == EPI_MODE_RESIDUAL) {
+          bias_act32<0>(v0, p.bias, nb0);
+          bias_act32<0>(v1, p.bias, nb0 + 32);
+          if (nc < p.N) {
+            if (!mbar_wait(&res_full[g], res_loads & 1u, 5)) *abort_flag = 1;
+            ++res_loads;
+            res_pending = false;
+          }
+          const uint8_t* srow = stile + r * 128;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const uint4 u = *reinterpret_cast<const uint4*>(srow + ((c ^ (r & 7)) * 16));
+            const __half2* h = reinterpret_cast<const __half2*>(&u);
+            float* v = c < 4 ? v0 : v1;
+            const int o = (c & 3) * 8;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = __half22float2(h[e]);
+              v[o + 2 * e] = f.x + f16r(v[o + 2 * e]);
+              v[o + 2 * e + 1] = f.y + f16r(v[o + 2 * e + 1]);
+            }
+          }
+        } else {
+          bias_act32<MODE>(v0, p.bias, nb0);
+          bias_act32<MODE>(v1, p.bias, nb0 + 32);
+          named_bar(1 + g, 128);
+        }
+        stage32_sw128(stile, r, 0, v0);
+        stage32_sw128(stile, r, 4, v1);
+        fence_proxy_async_smem();
+        named_bar(1 + g, 128);
+        if (leader) {
+          if (nc < p.N) tma_store_2d(&tmC, stile, nc, row0);
+          bulk_commit();
+        }
+      }
+    }
+    if (leader) {
+      if (res_pending) mbar_wait(&res_full[g], res_loads & 1u, 13);
+      bulk_wait<0>();
+    }
+  }
+  fence_before_sync();
+  cluster_sync();  // neither CTA leaves while the other may still use its shared memory or TMEM
+  if (warp == 1) {
+    fence_after_sync();
+    tmem_free_pair(tmem, G::TMEM_COLS);
+  }
+}
+
 }  // namespace
 
 bool gemm_tc_supported(int N, int K) { return N >= 64 && N % 64 == 0 && K % 8 == 0 && K >= 16; }
 bool gemm_tc_supported_geglu(int N, int K) { return N % 128 == 0 && gemm_tc_supported(N, K); }
 bool gemm_tc_supported_rope(int D) { return D == 64; }
 
-// Tile width of a GEMM with N outputs.
-static int tile_n(int N) { return N % 256 == 0 ? 256 : 128; }
+// Tile width of a GEMM with N outputs (CTA-pair tiles: 256 x BN).
+static int tile_n(int N) { return N % 256 == 0 ? 256 : (N % 192 == 0 ? 192 : 128); }
 
 int gemm_geglu_group(int N) { return tile_n(N) / 2; }
 
@@ -443,25 +782,102 @@ DevTensor gemm_geglu_bias(Ctx* ctx, const std::string& name, int N) {
   return d;
 }
 
-template <int BN>
-static void launch_bn(const void* A, const void* W, void* C, const Params& p, cudaStream_t st) {
+template <int BN, int MODE>
+static void launch_mode(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const Params& p,
+                        int grid, cudaStream_t st) {
   static bool configured = false;
   if (!configured) {
-    KH_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, GCfg<BN>::SMEM));
+    KH_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 GCfg<BN>::SMEM));
     configured = true;
   }
+  gemm_tc_kernel<BN, MODE><<<grid, GCfg<BN>::THREADS, GCfg<BN>::SMEM, st>>>(ma, mb, mc, p);
+}
+
+template <int BN, int MODE>
+static void launch_pair_mode(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const Params& p,
+                             int tiles, cudaStream_t st) {
+  static int max_pairs = 0;
+  if (max_pairs == 0) {
+    KH_CUDA(cudaFuncSetAttribute(gemm_pair_kernel<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 PCfg<BN>::SMEM));
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * device_sms(), 1, 1);
+    cfg.blockDim = dim3(PCfg<BN>::THREADS, 1, 1);
+    cfg.dynamicSmemBytes = PCfg<BN>::SMEM;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    KH_CUDA(cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<BN, MODE>, &cfg));
+    if (n <= 0) throw CudaError("gemm: no CTA pair fits on the device");
+    max_pairs = n;
+  }
+  const int pairs = std::min(tiles, max_pairs);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(PCfg<BN>::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = PCfg<BN>::SMEM;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  KH_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<BN, MODE>, ma, mb, mc, p));
+}
+
+template <int BN>
+static void launch_pair(const void* A, const void* W, void* C, const Params& p, int mode, cudaStream_t st) {
+  const int M = p.M, N = p.N, K = p.K;
+  const CUtensorMap& ma = tensor_map_f16(A, uint64_t(M), uint64_t(K), uint64_t(K), BK, BM, 128);
+  const CUtensorMap& mb = tensor_map_f16(W, uint64_t(N), uint64_t(K), uint64_t(K), BK, BN / 2, 128);
+  const CUtensorMap& mc = mode == EPI_MODE_GEGLU
+                              ? tensor_map_f16(C, uint64_t(M), uint64_t(N / 2), uint64_t(N / 2), 32, 128, 64)
+                              : tensor_map_f16(C, uint64_t(M), uint64_t(N), uint64_t(N), 64, 128, 128);
+  const int tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN);
+  switch (mode) {
+    case 0: launch_pair_mode<BN, 0>(ma, mb, mc, p, tiles, st); break;
+    case 1: launch_pair_mode<BN, 1>(ma, mb, mc, p, tiles, st); break;
+    case 2: launch_pair_mode<BN, 2>(ma, mb, mc, p, tiles, st); break;
+    case 3: launch_pair_mode<BN, 3>(ma, mb, mc, p, tiles, st); break;
+    case 4: launch_pair_mode<BN, 4>(ma, mb, mc, p, tiles, st); break;
+    case EPI_MODE_RESIDUAL: launch_pair_mode<BN, EPI_MODE_RESIDUAL>(ma, mb, mc, p, tiles, st); break;
+    case EPI_MODE_GEGLU: launch_pair_mode<BN, EPI_MODE_GEGLU>(ma, mb, mc, p, tiles, st); break;
+    case EPI_MODE_ROPE: launch_pair_mode<BN, EPI_MODE_ROPE>(ma, mb, mc, p, tiles, st); break;
+    default: throw PlanError("gemm: unknown epilogue mode");
+  }
+}
+
+template <int BN>
+static void launch_bn(const void* A, const void* W, void* C, const Params& p, int mode, cudaStream_t st) {
   const int M = p.M, N = p.N, K = p.K;
   const CUtensorMap& ma = tensor_map_f16(A, uint64_t(M), uint64_t(K), uint64_t(K), BK, BM, 128);
   const CUtensorMap& mb = tensor_map_f16(W, uint64_t(N), uint64_t(K), uint64_t(K), BK, BN, 128);
-  // output boxes: 64 columns (128-byte rows); GeGLU writes BN / 4 columns per warpgroup
-  const CUtensorMap& mc =
-      p.epi == EPI_GEGLU
-          ? tensor_map_f16(C, uint64_t(M), uint64_t(N / 2), uint64_t(N / 2), BN / 4, 128, BN / 4 * 2)
-          : tensor_map_f16(C, uint64_t(M), uint64_t(N), uint64_t(N), 64, 128, 128);
+  // output boxes: 64 columns (128-byte rows); GeGLU writes 32 columns (64-byte rows) per warpgroup
+  const CUtensorMap& mc = mode == EPI_MODE_GEGLU
+                              ? tensor_map_f16(C, uint64_t(M), uint64_t(N / 2), uint64_t(N / 2), 32, 128, 64)
+                              : tensor_map_f16(C, uint64_t(M), uint64_t(N), uint64_t(N), 64, 128, 128);
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   static const int sms = device_sms();
   const int grid = std::min(tiles, sms);
-  gemm_tc_kernel<BN><<<grid, THREADS, GCfg<BN>::SMEM, st>>>(ma, mb, mc, p);
+  switch (mode) {
+    case 0: launch_mode<BN, 0>(ma, mb, mc, p, grid, st); break;
+    case 1: launch_mode<BN, 1>(ma, mb, mc, p, grid, st); break;
+    case 2: launch_mode<BN, 2>(ma, mb, mc, p, grid, st); break;
+    case 3: launch_mode<BN, 3>(ma, mb, mc, p, grid, st); break;
+    case 4: launch_mode<BN, 4>(ma, mb, mc, p, grid, st); break;
+    case EPI_MODE_RESIDUAL: launch_mode<BN, EPI_MODE_RESIDUAL>(ma, mb, mc, p, grid, st); break;
+    case EPI_MODE_GEGLU: launch_mode<BN, EPI_MODE_GEGLU>(ma, mb, mc, p, grid, st); break;
+    case EPI_MODE_ROPE: launch_mode<BN, EPI_MODE_ROPE>(ma, mb, mc, p, grid, st); break;
+    default: throw PlanError("gemm: unknown epilogue mode");
+  }
 }
 
 void launch_gemm(Ctx* ctx, bool f16, const void* A, const void* W, const void* bias, void* C, int M, int N, int K,
@@ -473,33 +889,34 @@ void launch_gemm(Ctx* ctx, bool f16, const void* A, const void* W, const void* b
     launch_gemm_simt(f16, A, W, bias, C, M, N, K, act, st);
     return;
   }
+  if (act < 0 || act > 4) throw PlanError("gemm: unknown activation " + std::to_string(act));
   Params p;
   p.M = M;
   p.N = N;
   p.K = K;
   p.bias = static_cast<const __half*>(bias);
-  p.C = static_cast<const __half*>(C);
-  p.ldc = N;
-  p.act = act;
-  p.epi = EPI_PLAIN;
   p.table = nullptr;
   p.row_pos = nullptr;
   p.rope_cols = 0;
+  int mode = act;
   if (e.kind == GemmEpilogue::Residual) {
-    p.epi = EPI_RESIDUAL;
     if (act) throw PlanError("residual epilogue after an activation");
+    mode = EPI_MODE_RESIDUAL;
   } else if (e.kind == GemmEpilogue::GeGLU) {
-    p.epi = EPI_GEGLU;
-    p.ldc = N / 2;
+    if (act) throw PlanError("geglu epilogue after an activation");
+    mode = EPI_MODE_GEGLU;
   } else if (e.kind == GemmEpilogue::Rope) {
     if (e.D != 64) throw PlanError("rope epilogue needs 64-wide heads");
-    p.epi = EPI_ROPE;
+    if (act) throw PlanError("rope epilogue after an activation");
+    mode = EPI_MODE_ROPE;
     p.table = e.table;
     p.row_pos = e.row_pos;
     p.rope_cols = 2 * e.H * e.D;
   }
-  if (tile_n(N) == 256) launch_bn<256>(A, W, C, p, st);
-  else launch_bn<128>(A, W, C, p, st);
+  const int bn = tile_n(N);
+  if (bn == 256) launch_pair<256>(A, W, C, p, mode, st);
+  else if (bn == 192) launch_pair<192>(A, W, C, p, mode, st);
+  else launch_pair<128>(A, W, C, p, mode, st);
 }
 
 int tc_error_code() {

@@ -356,7 +356,7 @@ void plan_compile(Ctx* ctx, const Json& plan, CompiledPlan& cp) {
       std::string res_id, out_id = c_id;
       int out_cols = N;
       const std::string wname = bind(op, 1).substr(2);
-      if (f16 && !fixed_rows && i + 1 < ops.size() && gemm_tc_supported(N, K)) {
+      if (f16 && !fixed_rows && act == 0 && i + 1 < ops.size() && gemm_tc_supported(N, K)) {
         const Json& nx = *ops[i + 1];
         const std::string nk = nx["kernel"].as_str();
         if (nk == "add" && cint(nx, "MODE") == 0 && bind(nx, 1) == c_id) {
