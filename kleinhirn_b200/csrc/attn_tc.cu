@@ -13,16 +13,21 @@
 // sequences share a tile; a pair of rows from different sequences is masked. The keys of a tile
 // are the packed rows of every sequence its rows belong to (clamped to +-WINDOW around the tile
 // on windowed layers), in tiles of 128; which of them are present and unmasked is computed once
-// per CTA as bit masks. The CTA walks (head, key tile) items in order, 192 threads:
+// per CTA as bit masks. The CTA walks (head, key tile) items in order, 320 threads:
 //   warp 0     TMA: Q of each head, K and V of each item, into rings that run ahead across heads;
 //   warp 1     one thread issues S = Q K^T (M 128, N 128 keys, K = D) into TMEM columns
-//              [0, 128) and O = P V (M 128, N = D, K 128 keys, V as an MN-major operand) into
-//              TMEM columns [128, 128 + D); the next item's S is issued as soon as the softmax
-//              has read the current one, before the current PV;
-//   warps 2-5  softmax, one thread per query row (TMEM lane): scores in the log2 domain, running
-//              max and sum, P in f16 into shared memory (128-byte swizzled K-major rows), then
-//              the context row accumulated in registers: o = o * exp2(m_old - m_new) + O.
-// Two CTAs share an SM (256 TMEM columns and <= 102 KB of shared memory each).
+//              [0, 128) and O += P V (M 128, N = D, K 128 keys, V as an MN-major operand) into
+//              the head's O buffer, TMEM columns [128 + D (h % 2), 128 + D (h % 2) + D): O
+//              accumulates over the key tiles of a head in TMEM; the next item's S is issued as
+//              soon as the softmax has read the current one, before the current PV;
+//   warps 2-9  softmax, two threads per query row (TMEM lane), warps 2-5 on keys [0, 64) of
+//              each key tile and warps 6-9 on keys [64, 128): the scores in registers, the
+//              exponentials exp2(s - m) in the log2 domain against a reference point m that
+//              only moves when a tile's maximum exceeds it by more than 8 (then O is rescaled
+//              in TMEM, which is rare), P in f16 into shared memory (128-byte swizzled K-major
+//              rows); the two threads of a row exchange their maxima per item and their sums
+//              per head through shared memory; at the end of a head, ctx = O / sum.
+// Two CTAs share an SM (256 TMEM columns and <= 108 KB of shared memory each).
 
 #include <algorithm>
 
@@ -39,7 +44,7 @@ using namespace sm100;
 
 constexpr int TQ = 128;
 constexpr int TKEYS = 128;
-constexpr int THREADS = 192;
+constexpr int THREADS = 320;  // producer warp, MMA warp, 8 softmax warps (two per query row)
 constexpr uint32_t TMEM_COLS = 256;
 constexpr int MAXKT = 160;  // key tiles of one CTA: sequences up to 10,000 rows
 
@@ -55,7 +60,8 @@ struct Cfg {
   static constexpr int V_OFF = K_OFF + KS * TILE;
   static constexpr int P_OFF = V_OFF + VS * TILE;  // 2 blocks of 128 rows x 64 keys, 16 KB each
   static constexpr int BITS_OFF = P_OFF + 32768;   // present-and-unmasked / masked-key bits
-  static constexpr int BAR_OFF = BITS_OFF + 2 * MAXKT * 4 * 4;
+  static constexpr int XCH_OFF = BITS_OFF + 2 * MAXKT * 4 * 4;  // row max / sum exchange of the two halves
+  static constexpr int BAR_OFF = XCH_OFF + 2 * (4 * 2 * 2 * 128);  // xmax and xsum, f32 [2][2][128] each
   static constexpr int USED = BAR_OFF + 256;
   // at least 100 KB so that no more than two CTAs (2 x 256 TMEM columns) share an SM
   static constexpr int SMEM = (USED + 1024 > 102400 ? USED + 1024 : 102400);
@@ -91,6 +97,8 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
   uint8_t* sP = smem + C::P_OFF;
   uint32_t* vbits = reinterpret_cast<uint32_t*>(smem + C::BITS_OFF);  // [tile][4]: key present, unmasked
   uint32_t* hbits = vbits + MAXKT * 4;                                 // [tile][4]: key present, masked
+  float* xmax = reinterpret_cast<float*>(smem + C::XCH_OFF);           // [parity][half][row]
+  float* xsum = xmax + 2 * 2 * 128;                                    // [parity][half][row]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* q_full = bars;       // 2
   uint64_t* q_empty = bars + 2;  // 2
@@ -128,8 +136,8 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
       mbar_init(&v_empty[s], 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(s_empty, 128);
-    mbar_init(p_full, 128);
+    mbar_init(s_empty, 256);
+    mbar_init(p_full, 256);
     mbar_init(o_full, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -209,6 +217,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
       ok = NI > 0 && issue_s(0);
       for (int it = 0; it < NI && ok; ++it) {
         if (it + 1 < NI && !issue_s(it + 1)) { ok = false; break; }
+        const int hh = it / nkt, j = it - hh * nkt;
         const int vs = it % C::VS;
         if (*abort_flag || !mbar_wait(p_full, uint32_t(it & 1), 26) ||
             !mbar_wait(&v_full[vs], uint32_t(it / C::VS) & 1, 27)) {
@@ -216,11 +225,13 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
           break;
         }
         fence_after_sync();
+        // O of head hh accumulates over its key tiles, in the TMEM buffer of the head's parity
+        const uint32_t o_addr = tmem + 128 + uint32_t((hh & 1) * D);
         const uint64_t dv = desc_rows<D>(sV + vs * C::TILE);
 #pragma unroll
         for (int kk = 0; kk < TKEYS / 16; ++kk) {
           const uint64_t dp = desc_rows<64>(sP + (kk >> 2) * 16384) + uint64_t(2 * (kk & 3));
-          mma_f16(tmem + 128, dp, dv + uint64_t(2 * D * kk), idesc_o, kk ? 1u : 0u);
+          mma_f16(o_addr, dp, dv + uint64_t(2 * D * kk), idesc_o, (j | kk) ? 1u : 0u);
         }
         mma_commit(o_full);
         mma_commit(&v_empty[vs]);
@@ -232,20 +243,26 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
       }
     }
   } else {
+    // Two threads per query row: warps 2-5 take keys [0, 64) of every key tile, warps 6-9 keys
+    // [64, 128) (TMEM lanes follow warp % 4 in both). They agree on the row maximum through
+    // shared memory once per item and on the row sum once per head.
     const int quarter = warp & 3;
+    const int hf = (warp - 2) >> 2;           // half of the key tile
     const int r_local = quarter * 32 + lane;  // query row = TMEM lane
-    const int st = threadIdx.x - 64;          // key row this thread prepares
-    const int sw = st >> 5;                   // its word of a key tile's bit masks
+    const int tid = threadIdx.x - 64;         // 0 .. 255
+    const int pair_bar = 1 + quarter;         // named barrier of the two warps of this quarter
     // which key rows of every key tile are present and unmasked (computed once for all heads)
-    for (int j = 0; j < nkt; ++j) {
-      const int kk = kstart + j * TKEYS + st;
-      const bool have = kk < kend && kk < p.T;
-      const bool valid = have && p.mask[kk] > 0.5f;
-      const uint32_t vb = __ballot_sync(0xffffffffu, valid);
-      const uint32_t hb = __ballot_sync(0xffffffffu, have && !valid);
-      if (lane == 0) {
-        vbits[j * 4 + sw] = vb;
-        hbits[j * 4 + sw] = hb;
+    if (tid < 128) {
+      for (int j = 0; j < nkt; ++j) {
+        const int kk = kstart + j * TKEYS + tid;
+        const bool have = kk < kend && kk < p.T;
+        const bool valid = have && p.mask[kk] > 0.5f;
+        const uint32_t vb = __ballot_sync(0xffffffffu, valid);
+        const uint32_t hb = __ballot_sync(0xffffffffu, have && !valid);
+        if (lane == 0) {
+          vbits[j * 4 + (tid >> 5)] = vb;
+          hbits[j * 4 + (tid >> 5)] = hb;
+        }
       }
     }
     const int row = q0 + r_local;
@@ -262,149 +279,188 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
         hi = min(hi, row + p.window + 1);
       }
     }
-    named_bar(1, 128);
+    named_bar(5, 256);
     const uint32_t trow = tmem + (uint32_t(quarter * 32) << 16);
+    const int vrow = tid & 127, vpart = tid >> 7;  // value row (and its half) this thread clears
     bool ok = true;
-    // Items run in order; the PV product of item it is folded into the context only after the
-    // row maximum of item it + 1 is known, so its latency overlaps that pass. O of the last item
-    // of a head is folded in (and the head's context written) before the next head starts.
-    float m = -3.40282346638528859812e38f, l = 0.f, corr_prev = 1.f;
-    float o[D];
-#pragma unroll
-    for (int d = 0; d < D; ++d) o[d] = 0.f;
-    // folds O of item `it` (scaled state: o = o * corr + O) into the context row
-    auto fold = [&](int it, float corr) -> bool {
-      if (*abort_flag || !mbar_wait(o_full, uint32_t(it & 1), 43)) return false;
-      fence_after_sync();
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(trow + 128 + c * 32, r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[c * 32 + i] = fmaf(o[c * 32 + i], corr, __uint_as_float(r[i]));
+    // Running state of the current head (the same in both threads of a row): m = the reference
+    // point of the exponentials (scaled log2 units); m only moves when a key tile's maximum
+    // exceeds it by more than 8 (probabilities stay <= 2^8, exact in f16 up to the rounding),
+    // and then O in TMEM is rescaled before the tile's PV product. l = this thread's part of the
+    // row sum.
+    bool started = false;
+    float m = 0.f, l = 0.f;
+    auto wwait = [&](uint64_t* bar, uint32_t parity, int code) -> bool {
+      const bool r = !*abort_flag && mbar_wait(bar, parity, code);
+      return __all_sync(0xffffffffu, r);
+    };
+    // PV products observed complete so far. o_full completes once per PV, in order; the softmax
+    // observes every phase in order and has observed PV(it - 1) before it releases item it to
+    // the PV product, so the barrier is never two phases ahead of the phase waited for.
+    int o_done = 0;
+    auto wait_pv = [&](int it) -> bool {
+      while (o_done <= it) {
+        if (!wwait(o_full, uint32_t(o_done & 1), 43)) return false;
+        ++o_done;
       }
+      fence_after_sync();
       return true;
     };
+    // context row of head hh = O / l over this thread's D / 2 columns (a masked query row, or
+    // one without a kept key, is exactly zero: select, not multiply)
     auto finish_head = [&](int hh) {
-      if (!in_range) return;
-      // a masked query row, or one without a kept key, is exactly zero (select, not multiply)
-      const bool live = qvalid && l > 0.f;
-      const float inv = live ? 1.0f / l : 0.f;
-      uint4* dst = reinterpret_cast<uint4*>(p.ctx + int64_t(row) * H * D + int64_t(hg0 + hh) * D);
+      xsum[((hh & 1) * 2 + hf) * 128 + r_local] = l;
+      named_bar(pair_bar, 64);
+      const float lt = l + xsum[((hh & 1) * 2 + (hf ^ 1)) * 128 + r_local];
+      const bool live = qvalid && lt > 0.f;
+      const float inv = live ? 1.0f / lt : 0.f;
+      const uint32_t o_addr = trow + 128 + uint32_t((hh & 1) * D + hf * (D / 2));
+      uint4* dst = reinterpret_cast<uint4*>(p.ctx + int64_t(row) * H * D + int64_t(hg0 + hh) * D + hf * (D / 2));
 #pragma unroll
-      for (int q = 0; q < D / 8; ++q) {
+      for (int c = 0; c < D / 2; c += 8) {
+        uint32_t r[8];
+        tmem_ld8(o_addr + c, r);
+        tmem_ld_wait();
         __half2 hv[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e)
-          hv[e] = live ? __floats2half2_rn(o[q * 8 + 2 * e] * inv, o[q * 8 + 2 * e + 1] * inv)
+          hv[e] = live ? __floats2half2_rn(__uint_as_float(r[2 * e]) * inv, __uint_as_float(r[2 * e + 1]) * inv)
                        : __floats2half2_rn(0.f, 0.f);
-        dst[q] = *reinterpret_cast<uint4*>(hv);
+        if (in_range) dst[c / 8] = *reinterpret_cast<uint4*>(hv);
       }
     };
-    for (int it = 0; it < NI && ok; ++it) {
+    for (int it = 0; it < NI; ++it) {
       const int hh = it / nkt, j = it - hh * nkt;
-      const int k0 = kstart + j * TKEYS;
-      const bool holes = (hbits[j * 4] | hbits[j * 4 + 1] | hbits[j * 4 + 2] | hbits[j * 4 + 3]) != 0;
-      const int clo = min(max(lo - k0, 0), TKEYS), chi = min(max(hi - k0, 0), TKEYS);
-      if (*abort_flag || !mbar_wait(s_full, uint32_t(it & 1), 41)) { ok = false; break; }
-      fence_after_sync();
-      // pass 1: the row maximum of the kept raw scores (four independent chains)
-      float mr[4] = {-3.40282346638528859812e38f, -3.40282346638528859812e38f, -3.40282346638528859812e38f,
-                     -3.40282346638528859812e38f};
-#pragma unroll 1
-      for (int c4 = 0; c4 < 4; ++c4) {
-        const bool need = c4 * 32 < chi && c4 * 32 + 32 > clo;
-        if (!__any_sync(0xffffffffu, need)) continue;
-        uint32_t r[32];
-        tmem_ld32(trow + c4 * 32, r);
+      // A failed wait never ends one warp of a pair alone: the pair decides together at its
+      // named barriers (bar.red), so neither warp is left waiting at one.
+      bool fail = !ok;
+      if (j == 0 && it > 0) {  // a new head: write the previous one and start over
+        if (!fail) fail = !wait_pv(it - 1);
+        if (named_bar_any(pair_bar, 64, fail)) { ok = false; break; }
+        finish_head(hh - 1);
+        started = false;
+        l = 0.f;
+      }
+      const int k0 = kstart + j * TKEYS + hf * 64;  // first key of this thread's half
+      const int clo = min(max(lo - k0, 0), 64), chi = min(max(hi - k0, 0), 64);
+      // keep masks of this thread's two 32-key chunks: in the row's key range, present, unmasked
+      uint32_t km[2];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int a = min(max(clo - 32 * c, 0), 32), b = min(max(chi - 32 * c, 0), 32);
+        const uint32_t below_b = b >= 32 ? 0xffffffffu : ((1u << b) - 1u);
+        const uint32_t below_a = a >= 32 ? 0xffffffffu : ((1u << a) - 1u);
+        km[c] = (below_b & ~below_a) & vbits[j * 4 + hf * 2 + c];
+      }
+      if (!fail) fail = !wwait(s_full, uint32_t(it & 1), 41);
+      uint32_t sr[64];
+      if (!fail) {
+        fence_after_sync();
+        tmem_ld32(trow + hf * 64, *reinterpret_cast<uint32_t(*)[32]>(sr));
+        tmem_ld32(trow + hf * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
         tmem_ld_wait();
-        if (!need) continue;
-        if (!holes && clo <= c4 * 32 && c4 * 32 + 32 <= chi) {
+        fence_before_sync();
+        mbar_arrive(s_empty);  // S in TMEM is free for the next item
+      } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) mr[i & 3] = fmaxf(mr[i & 3], __uint_as_float(r[i]));
-        } else {
-          const uint32_t vw = holes ? vbits[j * 4 + c4] : 0xffffffffu;
+        for (int i = 0; i < 64; ++i) sr[i] = 0u;
+      }
+      // the row maximum of the kept raw scores: this half, then both halves
+      float mr[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int c = c4 * 32 + i;
-            if (c >= clo && c < chi && ((vw >> i) & 1u)) mr[i & 3] = fmaxf(mr[i & 3], __uint_as_float(r[i]));
-          }
+      for (int c = 0; c < 2; ++c) {
+        if (!__any_sync(0xffffffffu, km[c] != 0u)) continue;
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          mr[i & 3] = fmaxf(mr[i & 3], ((km[c] >> i) & 1u) ? __uint_as_float(sr[32 * c + i]) : -INFINITY);
+      }
+      const float pm = fmaxf(fmaxf(mr[0], mr[1]), fmaxf(mr[2], mr[3]));
+      float* xm = xmax + ((it & 1) * 2) * 128;
+      xm[hf * 128 + r_local] = pm;
+      if (named_bar_any(pair_bar, 64, fail)) { ok = false; break; }
+      const float mraw = fmaxf(pm, xm[(hf ^ 1) * 128 + r_local]);
+      float corr = 1.f;
+      if (mraw > -INFINITY) {
+        const float cand = mraw * p.scale_log2;
+        if (!started) {
+          m = cand;
+          started = true;
+        } else if (cand > m + 8.f) {
+          corr = ex2_approx(m - cand);
+          m = cand;
         }
       }
-      // the previous item's PV is done by now: fold it in (P and O are free again)
-      if (it > 0) {
-        if (!fold(it - 1, corr_prev)) { ok = false; break; }
-        if (j == 0) {  // a new head: write the previous one and start over
-          finish_head(hh - 1);
-          m = -3.40282346638528859812e38f;
-          l = 0.f;
-#pragma unroll
-          for (int d = 0; d < D; ++d) o[d] = 0.f;
-        }
+      // P of the previous item is free once its PV product is done (it has long been, as a
+      // rule); this also keeps the observed PV phases at most one behind
+      if (it >= 1 && !wait_pv(it - 1)) {
+        ok = false;  // the pair ends together at the next item's barrier
+        *abort_flag = 1;
+        continue;
       }
-      const float mraw = fmaxf(fmaxf(mr[0], mr[1]), fmaxf(mr[2], mr[3]));
-      const float mx = fmaxf(m, mraw * p.scale_log2);
-      const float corr = ex2_approx(m - mx);
-      float ls[4] = {0.f, 0.f, 0.f, 0.f};
-      // pass 2: p = exp2(s scale log2e - max) in f16, into this row of P (128-byte swizzled)
+      if (__any_sync(0xffffffffu, corr != 1.f)) {
+        // rescale this thread's columns of O (the PV products so far) before this item's PV
+        const uint32_t o_addr = trow + 128 + uint32_t((hh & 1) * D + hf * (D / 2));
 #pragma unroll 1
-      for (int c4 = 0; c4 < 4; ++c4) {
-        const bool need = c4 * 32 < chi && c4 * 32 + 32 > clo;
-        uint32_t packed[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) packed[i] = 0u;
-        if (__any_sync(0xffffffffu, need)) {
-          uint32_t r[32];
-          tmem_ld32(trow + c4 * 32, r);
+        for (int c = 0; c < D / 2; c += 8) {
+          uint32_t r[8];
+          tmem_ld8(o_addr + c, r);
           tmem_ld_wait();
-          if (need) {
-            const bool whole = !holes && clo <= c4 * 32 && c4 * 32 + 32 <= chi;
-            const uint32_t vw = holes ? vbits[j * 4 + c4] : 0xffffffffu;
 #pragma unroll
-            for (int i = 0; i < 32; i += 2) {
+          for (int e = 0; e < 8; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * corr);
+          tmem_st8(o_addr + c, r);
+        }
+        tmem_st_wait();
+        l *= corr;
+      }
+      // p = exp2(s scale log2e - m) in f16, into this row of P block hf (128-byte swizzled)
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};
+      uint8_t* prow = sP + hf * 16384 + r_local * 128;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const uint32_t k = km[c];
+        const bool any = __any_sync(0xffffffffu, k != 0u);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {  // keys 8 q .. 8 q + 7 of the chunk: one 16-byte chunk of P
+          uint32_t pk[4] = {0u, 0u, 0u, 0u};
+          if (any) {
+#pragma unroll
+            for (int e2 = 0; e2 < 4; ++e2) {
               float pv[2];
 #pragma unroll
               for (int e = 0; e < 2; ++e) {
-                const int c = c4 * 32 + i + e;
-                const bool keep = whole || (c >= clo && c < chi && ((vw >> (i + e)) & 1u));
-                pv[e] = keep ? ex2_approx(fmaf(__uint_as_float(r[i + e]), p.scale_log2, -mx)) : 0.f;
-                ls[(i + e) & 3] += pv[e];
+                const int i = 8 * q + 2 * e2 + e;
+                const float x = ex2_approx(fmaf(__uint_as_float(sr[32 * c + i]), p.scale_log2, -m));
+                pv[e] = ((k >> i) & 1u) ? x : 0.f;
+                ls[i & 3] += pv[e];
               }
               __half2 hv = __floats2half2_rn(pv[0], pv[1]);
-              packed[i / 2] = *reinterpret_cast<uint32_t*>(&hv);
+              pk[e2] = *reinterpret_cast<uint32_t*>(&hv);
             }
           }
-        }
-        // keys c4*32 .. +31: block c4/2, 16-byte chunks 4 (c4 % 2) .. +3 of this row, swizzled
-        uint8_t* prow = sP + (c4 >> 1) * 16384 + r_local * 128;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int ch = (c4 & 1) * 4 + q;
-          *reinterpret_cast<uint4*>(prow + ((ch ^ (r_local & 7)) * 16)) =
-              make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+          const int ch = c * 4 + q;
+          *reinterpret_cast<uint4*>(prow + ((ch ^ (r_local & 7)) * 16)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
       }
-      l = l * corr + ((ls[0] + ls[1]) + (ls[2] + ls[3]));
-      m = mx;
-      corr_prev = corr;
-      fence_before_sync();
-      mbar_arrive(s_empty);
+      l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
       // value rows of masked or absent keys become zero before the PV product
       const int vs = it % C::VS;
-      if (*abort_flag || !mbar_wait(&v_full[vs], uint32_t(it / C::VS) & 1, 42)) { ok = false; break; }
-      if (!((vbits[j * 4 + sw] >> (st & 31)) & 1u)) {
-        uint4* vrow = reinterpret_cast<uint4*>(sV + vs * C::TILE + st * C::ROW_BYTES);
+      if (!wwait(&v_full[vs], uint32_t(it / C::VS) & 1, 42)) {
+        ok = false;
+        *abort_flag = 1;
+        continue;
+      }
+      if (!((vbits[j * 4 + (vrow >> 5)] >> (vrow & 31)) & 1u)) {
+        uint4* vr = reinterpret_cast<uint4*>(sV + vs * C::TILE + vrow * C::ROW_BYTES + vpart * (C::ROW_BYTES / 2));
 #pragma unroll
-        for (int q = 0; q < C::ROW_BYTES / 16; ++q) vrow[q] = make_uint4(0, 0, 0, 0);
+        for (int q = 0; q < C::ROW_BYTES / 32; ++q) vr[q] = make_uint4(0, 0, 0, 0);
       }
       fence_proxy_async_smem();
+      fence_before_sync();
       mbar_arrive(p_full);
     }
-    if (ok && NI > 0) {
-      ok = fold(NI - 1, corr_prev);
-      if (ok) finish_head(HG - 1);
-    }
+    if (ok && NI > 0) ok = wait_pv(NI - 1);
+    if (named_bar_any(pair_bar, 64, !ok)) ok = false;
+    else if (NI > 0) finish_head(HG - 1);
     if (!ok) *abort_flag = 1;
   }
   fence_before_sync();

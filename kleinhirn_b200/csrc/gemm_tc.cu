@@ -51,17 +51,6 @@ constexpr int BK = 64;
 constexpr int A_BYTES = BM * BK * 2;
 constexpr int OUT_BYTES = 128 * 64 * 2;  // one warpgroup's staged output tile
 
-template <int BN>
-struct GCfg {
-  static constexpr int STAGES = BN == 256 ? 3 : 4;
-  static constexpr int B_BYTES = BN * BK * 2;
-  static constexpr uint32_t TMEM_COLS = 2 * BN;
-  static constexpr int NWG = BN / 64;                // epilogue warpgroups, 64 columns each
-  static constexpr int THREADS = 64 + 128 * NWG;     // producer warp, MMA warp, epilogue
-  static constexpr int SBUF = BN == 256 ? 1 : 2;     // staging tiles per warpgroup
-  static constexpr int SMEM = STAGES * (A_BYTES + B_BYTES) + NWG * SBUF * OUT_BYTES + 1024 + 256;
-};
-
 // Epilogue modes (compile time): 0-4 plain with activation ACT, then the fused follow-up ops.
 enum EpiMode { EPI_MODE_RESIDUAL = 5, EPI_MODE_GEGLU = 6, EPI_MODE_ROPE = 7 };
 
@@ -94,22 +83,6 @@ __device__ __forceinline__ float act_fn(float v, int act) {
 }
 
 __device__ __forceinline__ float f16r(float v) { return __half2float(__float2half_rn(v)); }
-
-// 32 consecutive f16 values of a row (16-byte aligned) as f32
-__device__ __forceinline__ void load32h(const __half* src, float (&v)[32]) {
-  const uint4* s = reinterpret_cast<const uint4*>(src);
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const uint4 u = s[q];
-    const __half2* h = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 f = __half22float2(h[e]);
-      v[q * 8 + 2 * e] = f.x;
-      v[q * 8 + 2 * e + 1] = f.y;
-    }
-  }
-}
 
 // Row r of a staged tile with 128-byte rows (128-byte swizzle, the TMA layout of a 64-column
 // f16 box): the 16-byte chunks ch .. ch + 3 hold v[0 .. 31].
@@ -156,278 +129,6 @@ __device__ __forceinline__ void bias_act32(float (&v)[32], const __half* bias, i
   if constexpr (MODE >= 1 && MODE <= 4) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = act_fn(v[i], MODE);
-  }
-}
-
-template <int BN, int MODE>
-__global__ void __launch_bounds__(GCfg<BN>::THREADS, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmC, const Params p) {
-  using G = GCfg<BN>;
-  constexpr int STAGES = G::STAGES;
-  constexpr int NWG = G::NWG;
-  constexpr int SBUF = G::SBUF;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * A_BYTES;
-  uint8_t* sOut = sB + STAGES * G::B_BYTES;  // [warpgroup][SBUF] 16 KB staging tiles
-  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + NWG * SBUF * OUT_BYTES);
-  uint64_t* empty = full + STAGES;
-  uint64_t* tfull = empty + STAGES;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* res_full = tempty + 2;  // [warpgroup]: residual tile landed in the staging tile
-  uint64_t* drain = res_full + NWG;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m_tiles = (p.M + BM - 1) / BM, n_tiles = (p.N + BN - 1) / BN;
-  const int tiles = m_tiles * n_tiles;
-  const int nk = (p.K + BK - 1) / BK;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 128 * NWG);
-    }
-    for (int g = 0; g < NWG; ++g) mbar_init(&res_full[g], 1);
-    mbar_init(drain, 1);
-    *abort_flag = 0;
-    fence_barrier_init();
-    prefetch_tmap(&tmA);
-    prefetch_tmap(&tmB);
-    prefetch_tmap(&tmC);
-  }
-  if (warp == 1) tmem_alloc(tmem_holder, G::TMEM_COLS);
-  fence_before_sync();
-  __syncthreads();
-  fence_after_sync();
-  const uint32_t tmem = *tmem_holder;
-
-  if (warp == 0) {
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      uint32_t issued = 0, last_parity = 0;  // stages with a load issued, parity of their last load
-      bool ok = true;
-      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-        const int mb = t / n_tiles, nb = t % n_tiles;
-        for (int kb = 0; kb < nk; ++kb) {
-          if (*abort_flag || !mbar_wait(&empty[stage], phase ^ 1, 1)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(&full[stage], A_BYTES + G::B_BYTES);
-          tma_load_2d(sA + stage * A_BYTES, &tmA, &full[stage], kb * BK, mb * BM);
-          tma_load_2d(sB + stage * G::B_BYTES, &tmB, &full[stage], kb * BK, nb * BN);
-          issued |= 1u << stage;
-          last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1;
-          }
-        }
-      }
-      if (!ok) {
-        *abort_flag = 1;
-        // let every copy this thread issued land before the CTA ends
-        for (int s = 0; s < STAGES; ++s)
-          if (issued & (1u << s)) mbar_wait(&full[s], (last_parity >> s) & 1u, 11);
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t idesc = idesc_f16(BM, BN);
-      int stage = 0;
-      uint32_t phase = 0;
-      int local = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++local) {
-        const int buf = local & 1;
-        const uint32_t tphase = (local >> 1) & 1;
-        if (*abort_flag || !mbar_wait(&tempty[buf], tphase ^ 1, 2)) {
-          ok = false;
-          break;
-        }
-        fence_after_sync();
-        const uint32_t d = tmem + uint32_t(buf * BN);
-        for (int kb = 0; kb < nk; ++kb) {
-          if (*abort_flag || !mbar_wait(&full[stage], phase, 3)) {
-            ok = false;
-            break;
-          }
-          fence_after_sync();
-          const uint64_t da = desc_sw128(sA + stage * A_BYTES);
-          const uint64_t db = desc_sw128(sB + stage * G::B_BYTES);
-#pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            mma_f16(d, da + uint64_t(k * 2), db + uint64_t(k * 2), idesc, (kb | k) != 0 ? 1u : 0u);
-          mma_commit(&empty[stage]);
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1;
-          }
-        }
-        if (!ok) break;
-        mma_commit(&tfull[buf]);
-      }
-      if (!ok) {
-        *abort_flag = 1;
-        mma_commit(drain);  // wait for the MMAs in flight before the TMEM is freed
-        mbar_wait(drain, 0, 12);
-      }
-    }
-  } else {
-    // epilogue warpgroup g owns accumulator columns [64 g, 64 g + 64) of every tile
-    const int q = warp & 3;          // TMEM lane quarter of this warp
-    const int g = (warp - 2) >> 2;   // warpgroup
-    const int r = q * 32 + lane;     // row of the tile
-    const bool leader = (warp == 2 + 4 * g) && lane == 0;
-    bool res_pending = false;        // a residual load of the leader not yet waited for
-    uint32_t res_loads = 0;          // residual loads of this warpgroup so far (barrier parity)
-    int local = 0;
-    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
-      const int buf = local & 1;
-      const uint32_t tphase = (local >> 1) & 1;
-      const int mb = t / n_tiles, nb = t % n_tiles;
-      const int row = mb * BM + r;
-      const bool live = row < p.M;
-      const int n0 = nb * BN;
-      uint8_t* stile = sOut + (g * SBUF + (local % SBUF)) * OUT_BYTES;
-      const int nc = n0 + g * 64;  // first output column of this warpgroup (plain, residual, rope)
-      // the TMA store that last read this staging tile must be done with it
-      if (leader) {
-        bulk_wait_read<SBUF - 1>();
-        if (MODE == EPI_MODE_RESIDUAL && nc < p.N) {
-          // the residual rows of the tile come in by TMA, into the staging tile
-          mbar_arrive_expect_tx(&res_full[g], OUT_BYTES);
-          tma_load_2d(stile, &tmC, &res_full[g], nc, mb * BM);
-          res_pending = true;
-        }
-      }
-      const bool failed = *abort_flag || !mbar_wait(&tfull[buf], tphase, 4);
-      // the warpgroup leaves together, so no thread is left waiting at its named barriers
-      if (named_bar_any(1 + g, 128, failed)) {
-        *abort_flag = 1;
-        break;
-      }
-      fence_after_sync();
-      const uint32_t taddr = tmem + (uint32_t(q * 32) << 16) + uint32_t(buf * BN);
-      if constexpr (MODE == EPI_MODE_GEGLU) {
-        // accumulator columns [0, BN/2) hold a, [BN/2, BN) hold b for the tile's BN/2 outputs;
-        // this warpgroup writes outputs [32 g, 32 g + 32) of the tile
-        uint32_t ra[32], rb[32];
-        tmem_ld32(taddr + g * 32, ra);
-        tmem_ld32(taddr + BN / 2 + g * 32, rb);
-        tmem_ld_wait();
-        fence_before_sync();
-        mbar_arrive(&tempty[buf]);  // the accumulator is read: the MMA may reuse it
-        named_bar(1 + g, 128);      // the staging tile is free
-        float a[32], b[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          a[i] = __uint_as_float(ra[i]);
-          b[i] = __uint_as_float(rb[i]);
-        }
-        bias_act32<0>(a, p.bias, n0 + g * 32);
-        bias_act32<0>(b, p.bias, n0 + BN / 2 + g * 32);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) a[i] = gelu_as(f16r(a[i])) * f16r(b[i]);
-        stage32_sw64(stile, r, a);
-        fence_proxy_async_smem();
-        named_bar(1 + g, 128);
-        if (leader) {
-          tma_store_2d(&tmC, stile, nb * (BN / 2) + g * 32, mb * BM);
-          bulk_commit();
-        }
-      } else {
-        uint32_t r0[32], r1[32];
-        tmem_ld32(taddr + g * 64, r0);
-        tmem_ld32(taddr + g * 64 + 32, r1);
-        tmem_ld_wait();
-        fence_before_sync();
-        mbar_arrive(&tempty[buf]);  // the accumulator is read: the MMA may reuse it
-        float v0[32], v1[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          v0[i] = __uint_as_float(r0[i]);
-          v1[i] = __uint_as_float(r1[i]);
-        }
-        const int nb0 = min(nc, p.N - 64);  // bias columns stay inside N (N % 64 == 0)
-        if constexpr (MODE == EPI_MODE_ROPE) {
-          bias_act32<0>(v0, p.bias, nb0);
-          bias_act32<0>(v1, p.bias, nb0 + 32);
-          if (nc < p.rope_cols) {
-            // one 64-wide head: rotate-half with the table row of the local position
-            const float4* tb = reinterpret_cast<const float4*>(p.table + int64_t(live ? p.row_pos[row] : 0) * 128);
-#pragma unroll
-            for (int d4 = 0; d4 < 8; ++d4) {
-              const float4 c4 = __ldg(tb + d4), s4 = __ldg(tb + 16 + d4);
-              const float cs[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int d = d4 * 4 + e;
-                const float x = f16r(v0[d]), y = f16r(v1[d]);
-                v0[d] = x * cs[e] - y * sn[e];
-                v1[d] = y * cs[e] + x * sn[e];
-              }
-            }
-          }
-          named_bar(1 + g, 128);  // the staging tile is free
-        } else if constexpr (MODE == EPI_MODE_RESIDUAL) {
-          bias_act32<0>(v0, p.bias, nb0);
-          bias_act32<0>(v1, p.bias, nb0 + 32);
-          if (nc < p.N) {  // every thread sees the residual tile land
-            if (!mbar_wait(&res_full[g], res_loads & 1u, 5)) *abort_flag = 1;
-            ++res_loads;
-            res_pending = false;
-          }
-          // residual row r of the staged tile (128-byte swizzle): C + f16(acc + bias)
-          const uint8_t* srow = stile + r * 128;
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            const uint4 u = *reinterpret_cast<const uint4*>(srow + ((c ^ (r & 7)) * 16));
-            const __half2* h = reinterpret_cast<const __half2*>(&u);
-            float* v = c < 4 ? v0 : v1;
-            const int o = (c & 3) * 8;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 f = __half22float2(h[e]);
-              v[o + 2 * e] = f.x + f16r(v[o + 2 * e]);
-              v[o + 2 * e + 1] = f.y + f16r(v[o + 2 * e + 1]);
-            }
-          }
-        } else {
-          bias_act32<MODE>(v0, p.bias, nb0);
-          bias_act32<MODE>(v1, p.bias, nb0 + 32);
-          named_bar(1 + g, 128);  // the staging tile is free
-        }
-        stage32_sw128(stile, r, 0, v0);
-        stage32_sw128(stile, r, 4, v1);
-        fence_proxy_async_smem();
-        named_bar(1 + g, 128);
-        if (leader) {
-          if (nc < p.N) tma_store_2d(&tmC, stile, nc, mb * BM);
-          bulk_commit();
-        }
-      }
-    }
-    if (leader) {
-      // a residual load issued for a tile the loop left early must land before the CTA ends
-      if (res_pending) mbar_wait(&res_full[g], res_loads & 1u, 13);
-      bulk_wait<0>();
-    }
-  }
-  fence_before_sync();
-  __syncthreads();
-  if (warp == 1) {
-    fence_after_sync();
-    tmem_free(tmem, G::TMEM_COLS);
   }
 }
 
@@ -783,18 +484,6 @@ DevTensor gemm_geglu_bias(Ctx* ctx, const std::string& name, int N) {
 }
 
 template <int BN, int MODE>
-static void launch_mode(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const Params& p,
-                        int grid, cudaStream_t st) {
-  static bool configured = false;
-  if (!configured) {
-    KH_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 GCfg<BN>::SMEM));
-    configured = true;
-  }
-  gemm_tc_kernel<BN, MODE><<<grid, GCfg<BN>::THREADS, GCfg<BN>::SMEM, st>>>(ma, mb, mc, p);
-}
-
-template <int BN, int MODE>
 static void launch_pair_mode(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const Params& p,
                              int tiles, cudaStream_t st) {
   static int max_pairs = 0;
@@ -851,31 +540,6 @@ static void launch_pair(const void* A, const void* W, void* C, const Params& p, 
     case EPI_MODE_RESIDUAL: launch_pair_mode<BN, EPI_MODE_RESIDUAL>(ma, mb, mc, p, tiles, st); break;
     case EPI_MODE_GEGLU: launch_pair_mode<BN, EPI_MODE_GEGLU>(ma, mb, mc, p, tiles, st); break;
     case EPI_MODE_ROPE: launch_pair_mode<BN, EPI_MODE_ROPE>(ma, mb, mc, p, tiles, st); break;
-    default: throw PlanError("gemm: unknown epilogue mode");
-  }
-}
-
-template <int BN>
-static void launch_bn(const void* A, const void* W, void* C, const Params& p, int mode, cudaStream_t st) {
-  const int M = p.M, N = p.N, K = p.K;
-  const CUtensorMap& ma = tensor_map_f16(A, uint64_t(M), uint64_t(K), uint64_t(K), BK, BM, 128);
-  const CUtensorMap& mb = tensor_map_f16(W, uint64_t(N), uint64_t(K), uint64_t(K), BK, BN, 128);
-  // output boxes: 64 columns (128-byte rows); GeGLU writes 32 columns (64-byte rows) per warpgroup
-  const CUtensorMap& mc = mode == EPI_MODE_GEGLU
-                              ? tensor_map_f16(C, uint64_t(M), uint64_t(N / 2), uint64_t(N / 2), 32, 128, 64)
-                              : tensor_map_f16(C, uint64_t(M), uint64_t(N), uint64_t(N), 64, 128, 128);
-  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-  static const int sms = device_sms();
-  const int grid = std::min(tiles, sms);
-  switch (mode) {
-    case 0: launch_mode<BN, 0>(ma, mb, mc, p, grid, st); break;
-    case 1: launch_mode<BN, 1>(ma, mb, mc, p, grid, st); break;
-    case 2: launch_mode<BN, 2>(ma, mb, mc, p, grid, st); break;
-    case 3: launch_mode<BN, 3>(ma, mb, mc, p, grid, st); break;
-    case 4: launch_mode<BN, 4>(ma, mb, mc, p, grid, st); break;
-    case EPI_MODE_RESIDUAL: launch_mode<BN, EPI_MODE_RESIDUAL>(ma, mb, mc, p, grid, st); break;
-    case EPI_MODE_GEGLU: launch_mode<BN, EPI_MODE_GEGLU>(ma, mb, mc, p, grid, st); break;
-    case EPI_MODE_ROPE: launch_mode<BN, EPI_MODE_ROPE>(ma, mb, mc, p, grid, st); break;
     default: throw PlanError("gemm: unknown epilogue mode");
   }
 }

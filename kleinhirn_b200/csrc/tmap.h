@@ -12,6 +12,10 @@ namespace kh {
 const CUtensorMap& tensor_map_f16(const void* ptr, uint64_t rows, uint64_t cols, uint64_t row_stride,
                                   uint32_t box_cols, uint32_t box_rows, int swizzle_bytes);
 
+// The same map encoded into `out`, without the cache.
+void encode_tensor_map_f16(CUtensorMap* out, const void* ptr, uint64_t rows, uint64_t cols, uint64_t row_stride,
+                           uint32_t box_cols, uint32_t box_rows, int swizzle_bytes);
+
 int device_sms();
 
 }  // namespace kh
