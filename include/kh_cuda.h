@@ -159,6 +159,29 @@ void kh_bulk_destroy(kh_bulk* bulk);
  * its own events on it. The context owns the stream. */
 void* kh_ctx_stream(const kh_ctx* ctx);
 
+/* ---- allocation-free attention (no counterpart in the reference) ----
+ * Packed multi-head attention of f16 plans, what the attention ops of a standard-attention plan
+ * compute (src/kernels/attsoftmax.wgsl, mbattention.wgsl): per head softmax(scale q k^T) v over
+ * the rows of the same sequence, masked keys and keys outside +-window (0: no window) left out,
+ * masked query rows exactly zero. Caller-owned device buffers: qkv [T][3 * heads * head_dim]
+ * f16 (the q, k and v blocks of each row, as the plan's qkv buffer), mask [T] f32 (1 keep,
+ * 0 masked), ctx [T][heads * head_dim] f16 output; the T packed rows hold n_seqs sequences back
+ * to back, T = the sum of seq_lens (host memory).
+ *
+ * It allocates no device memory, on any call: its sequence table lives in a static device array
+ * of 563,200 bytes inside the library. It is for callers that cannot allocate at call time: a
+ * serving loop whose device memory is budgeted up front, or code that must not let a cudaMalloc
+ * synchronize the device in the middle of its work.
+ * Limits: n_seqs <= 4096, T <= 65,536, each length in [1, 10,176], head_dim 32 or 64, qkv and
+ * ctx 16-byte aligned; beyond them it returns KH_ERR_ARG and says which limit.
+ * The first call on a device does one-time set-up (looks up the static array, sets the kernel's
+ * shared-memory limit): make that call before any stream capture. All calls on a device share
+ * the static array: calls that overlap in time (other streams, other host threads) race on it,
+ * so the caller serializes them. The work is queued on `stream` (a cudaStream_t, NULL for the
+ * legacy default stream); the call returns once it is queued. */
+int kh_attention_f16_noalloc(const void* qkv, const float* mask, void* ctx, const int32_t* seq_lens, int n_seqs,
+                             int heads, int head_dim, float scale, int window, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -59,6 +59,8 @@ _SIGS = {
     "kh_bulk_destroy": ([_P], None),
     "kh_bulk_profile": ([_P, _P, ctypes.c_size_t], ctypes.c_int),
     "kh_ctx_stream": ([_P], ctypes.c_void_p),
+    "kh_attention_f16_noalloc": ([_P, _P, _P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float,
+                                  ctypes.c_int, _P], ctypes.c_int),
 }
 
 _lib = None
@@ -91,6 +93,16 @@ def load_library(path: Path | str | None = None):
 def _check(lib, status: int) -> None:
     if status != 0:
         raise KhError(status, lib.kh_last_error().decode("utf-8", "replace"))
+
+
+def attention_f16_noalloc(qkv_ptr: int, mask_ptr: int, ctx_ptr: int, seq_lens, heads: int, head_dim: int,
+                          scale: float, window: int = 0, stream: int = 0) -> None:
+    """kh_attention_f16_noalloc on device pointers (qkv f16 [T, 3 H D], mask f32 [T], ctx f16 [T, H D]);
+    seq_lens on the host, T = their sum. Queues the work on `stream` and allocates no device memory."""
+    lib = load_library()
+    lens = np.ascontiguousarray(seq_lens, dtype=np.int32)
+    _check(lib, lib.kh_attention_f16_noalloc(qkv_ptr, mask_ptr, ctx_ptr, lens.ctypes.data, len(lens), heads,
+                                              head_dim, scale, window, stream or None))
 
 
 def _ptr(a: np.ndarray | None):

@@ -683,4 +683,12 @@ void kh_bulk_destroy(kh_bulk* bulk) {
   delete bulk;
 }
 
+int kh_attention_f16_noalloc(const void* qkv, const float* mask, void* ctx, const int32_t* seq_lens, int n_seqs,
+                             int heads, int head_dim, float scale, int window, void* stream) {
+  return guard(nullptr, Latch::No, [&] {
+    kh::attention_f16_noalloc(qkv, mask, ctx, seq_lens, n_seqs, heads, head_dim, scale, window,
+                              static_cast<cudaStream_t>(stream));
+  });
+}
+
 }  // extern "C"

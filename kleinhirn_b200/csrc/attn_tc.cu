@@ -30,6 +30,8 @@
 // Two CTAs share an SM (256 TMEM columns and <= 108 KB of shared memory each).
 
 #include <algorithm>
+#include <mutex>
+#include <string>
 
 #include "attn_tc.h"
 #include "runtime.h"
@@ -502,7 +504,143 @@ void launch_tc(const AttnArgs& a, const SeqTable& seq, int T, cudaStream_t st) {
   attn_tc_kernel<D><<<grid, THREADS, Cfg<D>::SMEM, st>>>(tm, p);
 }
 
+// ---- packed attention whose sequence table lives in static device memory ----
+//
+// kh_attention_f16_noalloc runs the kernel above on caller-owned device buffers and keeps the
+// sequence table it needs in a file-scope device array, so the call allocates no device memory.
+// Limits: NA_MAX_ROWS packed rows and NA_MAX_SEQS sequences per call.
+
+constexpr int NA_MAX_ROWS = 65536;
+constexpr int NA_MAX_SEQS = 4096;
+constexpr int NA_LENS = 0;                                  // [NA_MAX_SEQS] lengths (from the host)
+constexpr int NA_START = NA_LENS + NA_MAX_SEQS;             // [NA_MAX_SEQS] first packed row
+constexpr int NA_ROWSEQ = NA_START + NA_MAX_SEQS;           // [NA_MAX_ROWS] sequence of each row
+constexpr int NA_PTILES = NA_ROWSEQ + NA_MAX_ROWS;          // [NA_MAX_ROWS / 128][3] packed tiles
+constexpr int NA_WORDS = NA_PTILES + 3 * (NA_MAX_ROWS / TQ);  // 140,800 words, 563,200 bytes
+
+// Every word a call reads is written earlier in the same call (lengths by the host copy, the rest
+// by the two setup kernels): nothing here has to start at zero.
+static __device__ __align__(256) int32_t kh_attn_noalloc_scratch[NA_WORDS];
+
+// One CTA of 1024 threads: exclusive prefix sum of the n <= 4096 lengths (sequence starts).
+__global__ void noalloc_starts_kernel(int32_t* w, int n) {
+  __shared__ int32_t part[1024];
+  const int per = (n + blockDim.x - 1) / blockDim.x;
+  const int b0 = threadIdx.x * per;
+  int32_t sum = 0;
+  for (int i = 0; i < per; ++i)
+    if (b0 + i < n) sum += w[NA_LENS + b0 + i];
+  part[threadIdx.x] = sum;
+  __syncthreads();
+  for (int off = 1; off < int(blockDim.x); off <<= 1) {
+    const int32_t v = int(threadIdx.x) >= off ? part[threadIdx.x - off] : 0;
+    __syncthreads();
+    part[threadIdx.x] += v;
+    __syncthreads();
+  }
+  int32_t run = part[threadIdx.x] - sum;
+  for (int i = 0; i < per; ++i)
+    if (b0 + i < n) {
+      w[NA_START + b0 + i] = run;
+      run += w[NA_LENS + b0 + i];
+    }
+}
+
+// Thread per packed row: its sequence, and for the first row of each 128-row tile the tile's key
+// range (its first row's sequence start to its last row's sequence end), as the plan path's
+// sequence table holds them.
+__global__ void noalloc_rows_kernel(int32_t* w, int n, int T) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= T) return;
+  auto seq_of = [&](int row) {
+    int lo = 0, hi = n - 1;  // lengths >= 1: starts strictly increase
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (w[NA_START + mid] <= row) lo = mid;
+      else hi = mid - 1;
+    }
+    return lo;
+  };
+  const int s = seq_of(r);
+  w[NA_ROWSEQ + r] = s;
+  if (r % TQ == 0) {
+    const int s1 = seq_of(min(T, r + TQ) - 1);
+    int32_t* pt = w + NA_PTILES + 3 * (r / TQ);
+    pt[0] = r;
+    pt[1] = w[NA_START + s];
+    pt[2] = w[NA_START + s1] + w[NA_LENS + s1];
+  }
+}
+
+// Address of the scratch array on the current device; the first call on a device looks it up
+// and sets the attention kernels' shared-memory limit.
+int32_t* noalloc_scratch() {
+  static std::mutex mu;
+  static int32_t* per_device[64] = {};
+  int dev = 0;
+  KH_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) throw ArgError("kh_attention_f16_noalloc: device ordinal above 63");
+  std::lock_guard<std::mutex> lk(mu);
+  if (!per_device[dev]) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, kh_attn_noalloc_scratch);
+    if (e != cudaSuccess)
+      throw CudaError(std::string("kh_attention_f16_noalloc: cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+    KH_CUDA(cudaFuncSetAttribute(attn_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<32>::SMEM));
+    KH_CUDA(cudaFuncSetAttribute(attn_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<64>::SMEM));
+    per_device[dev] = static_cast<int32_t*>(ptr);
+  }
+  return per_device[dev];
+}
+
 }  // namespace
+
+void attention_f16_noalloc(const void* qkv, const float* mask, void* ctx, const int32_t* seq_lens, int n_seqs,
+                           int H, int D, float scale, int window, cudaStream_t st) {
+  if (!qkv || !mask || !ctx || !seq_lens) throw ArgError("kh_attention_f16_noalloc: null pointer argument");
+  if (n_seqs < 1 || n_seqs > NA_MAX_SEQS)
+    throw ArgError("kh_attention_f16_noalloc: n_seqs " + std::to_string(n_seqs) + " outside [1, " +
+                   std::to_string(NA_MAX_SEQS) + "]");
+  if (D != 32 && D != 64) throw ArgError("kh_attention_f16_noalloc: head_dim must be 32 or 64");
+  if (H < 1) throw ArgError("kh_attention_f16_noalloc: heads must be >= 1");
+  if (window < 0) throw ArgError("kh_attention_f16_noalloc: window must be >= 0");
+  if ((reinterpret_cast<uintptr_t>(qkv) & 15) || (reinterpret_cast<uintptr_t>(ctx) & 15))
+    throw ArgError("kh_attention_f16_noalloc: qkv and ctx must be 16-byte aligned");
+  const int max_len = (MAXKT * TKEYS - TQ) / 2;
+  int64_t T = 0;
+  for (int i = 0; i < n_seqs; ++i) {
+    if (seq_lens[i] < 1 || seq_lens[i] > max_len)
+      throw ArgError("kh_attention_f16_noalloc: sequence length " + std::to_string(seq_lens[i]) + " outside [1, " +
+                     std::to_string(max_len) + "]");
+    T += seq_lens[i];
+  }
+  if (T > NA_MAX_ROWS)
+    throw ArgError("kh_attention_f16_noalloc: " + std::to_string(T) + " packed rows, at most " +
+                   std::to_string(NA_MAX_ROWS));
+  int32_t* w = noalloc_scratch();
+  KH_CUDA(cudaMemcpyAsync(w + NA_LENS, seq_lens, size_t(n_seqs) * 4, cudaMemcpyHostToDevice, st));
+  noalloc_starts_kernel<<<1, 1024, 0, st>>>(w, n_seqs);
+  noalloc_rows_kernel<<<int((T + 255) / 256), 256, 0, st>>>(w, n_seqs, int(T));
+  CUtensorMap tm;
+  const uint64_t cols = uint64_t(3) * H * D;
+  encode_tensor_map_f16(&tm, qkv, uint64_t(T), cols, cols, D, 128, D * 2);
+  Params p;
+  p.mask = mask;
+  p.seq_start = w + NA_START;
+  p.seq_len = w + NA_LENS;
+  p.row_seq = w + NA_ROWSEQ;
+  p.ptiles = w + NA_PTILES;
+  p.ctx = static_cast<__half*>(ctx);
+  p.H = H;
+  p.HG = heads_per_cta(H);
+  p.T = int(T);
+  p.window = window;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  const dim3 grid(unsigned((T + TQ - 1) / TQ), unsigned(H / p.HG));
+  if (D == 64) attn_tc_kernel<64><<<grid, THREADS, Cfg<64>::SMEM, st>>>(tm, p);
+  else attn_tc_kernel<32><<<grid, THREADS, Cfg<32>::SMEM, st>>>(tm, p);
+  KH_CUDA(cudaGetLastError());
+}
 
 int attention_tile_q(bool) { return 64; }
 

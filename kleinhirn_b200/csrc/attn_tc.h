@@ -14,4 +14,10 @@ void launch_attention(bool f16, const AttnArgs& a, const SeqTable& seq, cudaStre
 // Code of the first tensor-core attention wait that gave up (0: none); read after a sync.
 int attn_error_code();
 
+// Packed f16 attention over caller-owned device buffers with the sequence table in static device
+// memory (kh_attention_f16_noalloc): qkv [T, 3 H D], mask [T] f32, ctx [T, H D]; seq_lens on the
+// host, T = their sum. Throws ArgError beyond its limits.
+void attention_f16_noalloc(const void* qkv, const float* mask, void* ctx, const int32_t* seq_lens, int n_seqs,
+                           int H, int D, float scale, int window, cudaStream_t st);
+
 }  // namespace kh

@@ -13,7 +13,7 @@ HEADER = Path(__file__).resolve().parents[1] / "include" / "kh_cuda.h"
 
 def declared():
     text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
-    return sorted(set(re.findall(r"\b(kh_[a-z_]+)\s*\(", text)))
+    return sorted(set(re.findall(r"\b(kh_[a-z0-9_]+)\s*\(", text)))
 
 
 def test_header_declares_the_boundary():
