@@ -44,7 +44,7 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--pairs", type=int, default=65536)
-    ap.add_argument("--chunk-tokens", type=int, default=65536)
+    ap.add_argument("--chunk-tokens", type=int, default=262144)
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -331,7 +331,6 @@ def main():
         by_label[step["label"]] = by_label.get(step["label"], 0.0) + ms
     total_prof = sum(by_label.values())
     gemm_ms = by_label.get("gemm", 0.0)
-    gemm_launches = sum(1 for s, _ in prof if s["label"] == "gemm") * len(bulk_chunks(bulk))
     peaks = read_peaks()
     achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12 if gemm_ms > 0 else 0.0
     if args.profile_out and rank == 0:
@@ -373,12 +372,6 @@ def main():
     be.dispose()
     if dist:
         dist.destroy_process_group()
-
-
-def bulk_chunks(bulk) -> list:
-    """Number of chunks of the bulk's last set_lengths (launch groups per forward)."""
-    steps = len(bulk.runner.launches())
-    return [0] * max(1, bulk.last_timing()[1] // max(1, steps))
 
 
 if __name__ == "__main__":

@@ -371,10 +371,18 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
       float mr[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        if (!__any_sync(0xffffffffu, km[c] != 0u)) continue;
+        // warp-uniform cases: every lane keeps all 32 keys (no masks), none keeps any, or mixed
+        if (__all_sync(0xffffffffu, km[c] == 0xffffffffu)) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          mr[i & 3] = fmaxf(mr[i & 3], ((km[c] >> i) & 1u) ? __uint_as_float(sr[32 * c + i]) : -INFINITY);
+          for (int i = 0; i < 32; i += 2)
+            mr[(i >> 1) & 3] = fmax3(mr[(i >> 1) & 3], __uint_as_float(sr[32 * c + i]), __uint_as_float(sr[32 * c + i + 1]));
+        } else if (__any_sync(0xffffffffu, km[c] != 0u)) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 2)
+            mr[(i >> 1) & 3] = fmax3(mr[(i >> 1) & 3],
+                                     ((km[c] >> i) & 1u) ? __uint_as_float(sr[32 * c + i]) : -INFINITY,
+                                     ((km[c] >> (i + 1)) & 1u) ? __uint_as_float(sr[32 * c + i + 1]) : -INFINITY);
+        }
       }
       const float pm = fmaxf(fmaxf(mr[0], mr[1]), fmaxf(mr[2], mr[3]));
       float* xm = xmax + ((it & 1) * 2) * 128;
@@ -420,11 +428,23 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         const uint32_t k = km[c];
+        const bool all = __all_sync(0xffffffffu, k == 0xffffffffu);
         const bool any = __any_sync(0xffffffffu, k != 0u);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {  // keys 8 q .. 8 q + 7 of the chunk: one 16-byte chunk of P
           uint32_t pk[4] = {0u, 0u, 0u, 0u};
-          if (any) {
+          if (all) {
+#pragma unroll
+            for (int e2 = 0; e2 < 4; ++e2) {
+              const int i = 8 * q + 2 * e2;
+              const float x0 = ex2_approx(fmaf(__uint_as_float(sr[32 * c + i]), p.scale_log2, -m));
+              const float x1 = ex2_approx(fmaf(__uint_as_float(sr[32 * c + i + 1]), p.scale_log2, -m));
+              ls[i & 3] += x0;
+              ls[(i + 1) & 3] += x1;
+              __half2 hv = __floats2half2_rn(x0, x1);
+              pk[e2] = *reinterpret_cast<uint32_t*>(&hv);
+            }
+          } else if (any) {
 #pragma unroll
             for (int e2 = 0; e2 < 4; ++e2) {
               float pv[2];

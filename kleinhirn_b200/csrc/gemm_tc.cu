@@ -63,15 +63,22 @@ struct Params {
 };
 
 // GELU with the Abramowitz-Stegun 7.1.26 erf (the reference's formula and constants,
-// src/kernels/mmtile.wgsl:22-31); the reciprocal and exp through the MUFU approximations, whose
-// error is far below the f16 rounding of the stored result.
+// src/kernels/mmtile.wgsl:22-31): with u = v / sqrt(2), t = 1 / (1 + 0.3275911 |u|),
+// p(t) = t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) and erf|u| = 1 - p(t) exp(-u^2), the reference's
+// 0.5 v (1 + sign(v) erf|u|) equals relu(v) - 0.5 |v| p(t) exp(-v^2 / 2) for either sign of v,
+// which takes fewer operations: the 1/sqrt(2) goes into the t constant, the 0.5 into the
+// polynomial's coefficients. The reciprocal and exp use the MUFU approximations, whose error is
+// far below the f16 rounding of the stored result.
 __device__ __forceinline__ float gelu_as(float v) {
-  const float u = v * 0.7071067811865476f;
-  const float t = rcp_approx(1.0f + 0.3275911f * fabsf(u));
-  const float p = (((((1.061405429f * t - 1.453152027f) * t) + 1.421413741f) * t - 0.284496736f) * t +
-                   0.254829592f) * t;
-  const float e = 1.0f - p * ex2_approx(-(u * u) * 1.4426950408889634f);
-  return 0.5f * v * (1.0f + (v >= 0.0f ? e : -e));
+  const float a = fabsf(v);
+  const float t = rcp_approx(fmaf(a, 0.3275911f * 0.7071067811865476f, 1.0f));
+  float h = fmaf(0.5f * 1.061405429f, t, 0.5f * -1.453152027f);
+  h = fmaf(h, t, 0.5f * 1.421413741f);
+  h = fmaf(h, t, 0.5f * -0.284496736f);
+  h = fmaf(h, t, 0.5f * 0.254829592f);
+  const float hp = h * t;                                           // 0.5 p(t)
+  const float e = ex2_approx((v * v) * (-0.5f * 1.4426950408889634f));  // exp(-v^2 / 2)
+  return fmaf(-(a * hp), e, fmaxf(v, 0.0f));
 }
 
 __device__ __forceinline__ float act_fn(float v, int act) {
@@ -430,6 +437,308 @@ __global__ void __launch_bounds__(PCfg<BN>::THREADS, 1)
   }
 }
 
+// ---- GEMM + residual + LayerNorm (post-norm layers), on CTA pairs ----
+//
+// out = LayerNorm(R + round(A W^T + bias)) * w + b over rows of N = NF in {256, 384}: the matmul
+// whose output only feeds a mode-2 layernorm (src/plan/layers.ts:118-149, attnOut + lnA and
+// ffnOut + lnF) in one kernel. A pair owns whole 256-row tiles (all NF columns): two MMAs per
+// K = 16 step, N = NF / 2 each, accumulate into TMEM columns [0, NF/2) and [256, 256 + NF/2); each
+// CTA stages its 128 rows of the residual R by TMA into shared memory, and 16 epilogue warps
+// (four column quarters per TMEM lane quarter) take three passes over the accumulator: the row
+// sum, the sum of squared deviations (the reference's two-pass variance,
+// src/kernels/layernorm.wgsl:18-20), then the normalized f16 row, written over the staged R and
+// stored by TMA. One accumulator: the next tile's MMAs wait until the last pass has read it.
+template <int NF>
+struct LCfg {
+  static constexpr int NH = NF / 2;                 // N of each of the two MMAs
+  static constexpr int BQ = NF / 4;                 // W rows of one MMA staged per CTA
+  static constexpr int B_BYTES = 2 * BQ * BK * 2;   // both boxes
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int NBOX = NF / 64;              // 64-column boxes of a row tile
+  static constexpr int X_BYTES = NBOX * OUT_BYTES;  // 128 rows x NF f16: residual in, result out
+  static constexpr int STAGES = NF == 256 ? 4 : 3;
+  static constexpr int THREADS = 64 + 512;
+  static constexpr int RED_BYTES = 2 * 4 * 128 * 4;  // partial row sums [pass][quarter][row]
+  static constexpr int SMEM = STAGES * STAGE_BYTES + X_BYTES + RED_BYTES + 1024 + 256;
+  static constexpr int D1 = 256;                    // TMEM column of the second MMA's accumulator
+};
+
+struct LnParams {
+  int M, K;
+  const __half* bias;  // matmul bias (or null)
+  const __half* ln_w;
+  const __half* ln_b;  // (or null)
+  float eps;
+};
+
+template <int NF>
+__global__ void __launch_bounds__(LCfg<NF>::THREADS, 1)
+    gemm_addln_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const __grid_constant__ CUtensorMap tmR, const __grid_constant__ CUtensorMap tmO,
+                      const LnParams p) {
+  using G = LCfg<NF>;
+  constexpr int STAGES = G::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint8_t* sX = sB + STAGES * G::B_BYTES;  // [box][128 rows][128 bytes], 128-byte swizzle
+  float* red = reinterpret_cast<float*>(sX + G::X_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(red) + G::RED_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 1;
+  uint64_t* res_full = tempty + 1;
+  uint64_t* drain = res_full + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool first = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int tiles = (p.M + 2 * BM - 1) / (2 * BM);
+  const int nk = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tfull, 1);
+    mbar_init(tempty, 2 * 16);  // one arrival per epilogue warp of both CTAs
+    mbar_init(res_full, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+    prefetch_tmap(&tmR);
+    prefetch_tmap(&tmO);
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_holder, 512);
+  fence_before_sync();
+  cluster_sync();
+  fence_after_sync();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0, last_parity = 0;
+      bool ok = true;
+      for (int t = pair; t < tiles && ok; t += npairs) {
+        for (int kb = 0; kb < nk; ++kb) {
+          if (*abort_flag || !mbar_wait(&empty[stage], phase ^ 1, 51)) {
+            ok = false;
+            break;
+          }
+          if (first) mbar_arrive_expect_tx(&full[stage], 2 * G::STAGE_BYTES);
+          const uint32_t bar = cluster_addr(&full[stage], 0);
+          uint8_t* b = sB + stage * G::B_BYTES;
+          tma_load_2d_pair(sA + stage * A_BYTES, &tmA, bar, kb * BK, t * 2 * BM + int(rank) * BM);
+          tma_load_2d_pair(b, &tmB, bar, kb * BK, int(rank) * G::BQ);
+          tma_load_2d_pair(b + G::BQ * 128, &tmB, bar, kb * BK, G::NH + int(rank) * G::BQ);
+          issued |= 1u << stage;
+          last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        if (first)
+          for (int s = 0; s < STAGES; ++s)
+            if (issued & (1u << s)) mbar_wait(&full[s], (last_parity >> s) & 1u, 61);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && first) {
+      const uint32_t idesc = idesc_f16(2 * BM, G::NH);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = pair; t < tiles && ok; t += npairs, ++local) {
+        if (*abort_flag || !mbar_wait(tempty, uint32_t(local & 1) ^ 1, 52)) {
+          ok = false;
+          break;
+        }
+        fence_after_sync();
+        for (int kb = 0; kb < nk; ++kb) {
+          if (*abort_flag || !mbar_wait(&full[stage], phase, 53)) {
+            ok = false;
+            break;
+          }
+          fence_after_sync();
+          const uint64_t da = desc_sw128(sA + stage * A_BYTES);
+          const uint64_t db0 = desc_sw128(sB + stage * G::B_BYTES);
+          const uint64_t db1 = desc_sw128(sB + stage * G::B_BYTES + G::BQ * 128);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint32_t acc = (kb | k) != 0 ? 1u : 0u;
+            mma_f16_pair(tmem, da + uint64_t(k * 2), db0 + uint64_t(k * 2), idesc, acc);
+            mma_f16_pair(tmem + G::D1, da + uint64_t(k * 2), db1 + uint64_t(k * 2), idesc, acc);
+          }
+          mma_commit_pair_both(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit_pair_both(tfull);
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        mma_commit_pair(drain);
+        mbar_wait(drain, 0, 62);
+      }
+    }
+  } else {
+    // warp w: TMEM lanes 32 (w % 4) .. (its rows), columns [g NF/4, (g + 1) NF/4)
+    constexpr int QC = NF / 4;  // columns of one quarter: 64 or 96
+    const int q = warp & 3;
+    const int g = (warp - 2) >> 2;
+    const int r = q * 32 + lane;
+    const bool leader = warp == 2 && lane == 0;
+    const uint32_t trow = tmem + (uint32_t(q * 32) << 16);
+    float* red1 = red;            // [quarter][row]: sums
+    float* red2 = red + 4 * 128;  // [quarter][row]: squared deviations
+    bool res_pending = false;
+    int local = 0;
+    auto tcol = [&](int c0) { return trow + uint32_t(c0 < G::NH ? c0 : c0 - G::NH + G::D1); };
+    // v = round(acc + bias) + R for the 32 columns c0 .. c0 + 31 of row r, from the accumulator
+    auto make_v = [&](int c0, float (&v)[32]) {
+      uint32_t a[32];
+      tmem_ld32(tcol(c0), a);
+      tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(a[i]);
+      bias_act32<0>(v, p.bias, c0);
+      const uint8_t* xrow = sX + (c0 >> 6) * OUT_BYTES + r * 128;
+      const int ch0 = (c0 & 63) >> 3;
+#pragma unroll
+      for (int cq = 0; cq < 4; ++cq) {
+        const uint4 u = *reinterpret_cast<const uint4*>(xrow + (((ch0 + cq) ^ (r & 7)) * 16));
+        const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __half22float2(h[e]);
+          v[cq * 8 + 2 * e] = f16r(v[cq * 8 + 2 * e]) + f.x;
+          v[cq * 8 + 2 * e + 1] = f16r(v[cq * 8 + 2 * e + 1]) + f.y;
+        }
+      }
+    };
+    auto load_v = [&](int c0, float (&v)[32]) {
+      uint32_t a[32];
+      tmem_ld32(tcol(c0), a);
+      tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(a[i]);
+    };
+    for (int t = pair; t < tiles; t += npairs, ++local) {
+      const int row0 = t * 2 * BM + int(rank) * BM;
+      if (leader) {
+        bulk_wait_read<0>();  // the previous tile's result has left the staging tile
+        mbar_arrive_expect_tx(res_full, G::X_BYTES);
+#pragma unroll
+        for (int b = 0; b < G::NBOX; ++b) tma_load_2d(sX + b * OUT_BYTES, &tmR, res_full, b * 64, row0);
+        res_pending = true;
+      }
+      bool failed = *abort_flag || !mbar_wait(tfull, uint32_t(local & 1), 54);
+      failed = failed || !mbar_wait(res_full, uint32_t(local & 1), 55);
+      if (leader) res_pending = false;
+      if (named_bar_any(1, 512, failed)) {
+        *abort_flag = 1;
+        break;
+      }
+      fence_after_sync();
+      // pass 1: v into the accumulator's columns (f32), and the row sum
+      float s = 0.f;
+#pragma unroll 1
+      for (int cc = 0; cc < QC / 32; ++cc) {
+        const int c0 = g * QC + cc * 32;
+        float v[32];
+        make_v(c0, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s += v[i];
+        tmem_st32(tcol(c0), *reinterpret_cast<uint32_t(*)[32]>(v));
+      }
+      tmem_st_wait();
+      red1[g * 128 + r] = s;
+      named_bar(1, 512);
+      const float mean = ((red1[r] + red1[128 + r]) + (red1[256 + r] + red1[384 + r])) / float(NF);
+      // pass 2: squared deviations
+      float qs = 0.f;
+#pragma unroll 1
+      for (int cc = 0; cc < QC / 32; ++cc) {
+        float v[32];
+        load_v(g * QC + cc * 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float d = v[i] - mean;
+          qs += d * d;
+        }
+      }
+      red2[g * 128 + r] = qs;
+      named_bar(1, 512);
+      const float var = ((red2[r] + red2[128 + r]) + (red2[256 + r] + red2[384 + r])) / float(NF);
+      const float inv = 1.0f / sqrtf(var + p.eps);
+      // pass 3: (v - mean) inv w + b, over the staged residual
+#pragma unroll 1
+      for (int cc = 0; cc < QC / 32; ++cc) {
+        const int c0 = g * QC + cc * 32;
+        float v[32];
+        load_v(c0, v);
+        const uint4* wv = reinterpret_cast<const uint4*>(p.ln_w + c0);
+        const uint4* bv = reinterpret_cast<const uint4*>(p.ln_b + c0);
+        uint8_t* xrow = sX + (c0 >> 6) * OUT_BYTES + r * 128;
+        const int ch0 = (c0 & 63) >> 3;
+#pragma unroll
+        for (int cq = 0; cq < 4; ++cq) {
+          const uint4 wu = __ldg(wv + cq);
+          const uint4 bu = p.ln_b ? __ldg(bv + cq) : make_uint4(0, 0, 0, 0);
+          const __half2* wh = reinterpret_cast<const __half2*>(&wu);
+          const __half2* bh = reinterpret_cast<const __half2*>(&bu);
+          __half2 o[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 wf = __half22float2(wh[e]), bf = __half22float2(bh[e]);
+            o[e] = __floats2half2_rn((v[cq * 8 + 2 * e] - mean) * inv * wf.x + bf.x,
+                                     (v[cq * 8 + 2 * e + 1] - mean) * inv * wf.y + bf.y);
+          }
+          *reinterpret_cast<uint4*>(xrow + (((ch0 + cq) ^ (r & 7)) * 16)) = *reinterpret_cast<uint4*>(o);
+        }
+      }
+      // the accumulator is read: the MMAs of the next tile may start
+      fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(cluster_addr(tempty, 0));
+      fence_proxy_async_smem();
+      named_bar(1, 512);
+      if (leader) {
+#pragma unroll
+        for (int b = 0; b < G::NBOX; ++b) tma_store_2d(&tmO, sX + b * OUT_BYTES, b * 64, row0);
+        bulk_commit();
+      }
+    }
+    if (leader) {
+      if (res_pending) mbar_wait(res_full, uint32_t(local & 1), 63);
+      bulk_wait<0>();
+    }
+  }
+  fence_before_sync();
+  cluster_sync();
+  if (warp == 1) {
+    fence_after_sync();
+    tmem_free_pair(tmem, 512);
+  }
+}
+
 }  // namespace
 
 bool gemm_tc_supported(int N, int K) { return N >= 64 && N % 64 == 0 && K % 8 == 0 && K >= 16; }
@@ -581,6 +890,63 @@ void launch_gemm(Ctx* ctx, bool f16, const void* A, const void* W, const void* b
   if (bn == 256) launch_pair<256>(A, W, C, p, mode, st);
   else if (bn == 192) launch_pair<192>(A, W, C, p, mode, st);
   else launch_pair<128>(A, W, C, p, mode, st);
+}
+
+bool gemm_tc_supported_addln(int N, int K) { return (N == 256 || N == 384) && K % 8 == 0 && K >= 16; }
+
+template <int NF>
+static void launch_addln_nf(const void* A, const void* W, const void* R, void* O, const LnParams& p,
+                            cudaStream_t st) {
+  using G = LCfg<NF>;
+  static int max_pairs = 0;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  if (max_pairs == 0) {
+    KH_CUDA(cudaFuncSetAttribute(gemm_addln_kernel<NF>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * device_sms(), 1, 1);
+    cfg.blockDim = dim3(G::THREADS, 1, 1);
+    cfg.dynamicSmemBytes = G::SMEM;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    KH_CUDA(cudaOccupancyMaxActiveClusters(&n, gemm_addln_kernel<NF>, &cfg));
+    if (n <= 0) throw CudaError("gemm+layernorm: no CTA pair fits on the device");
+    max_pairs = n;
+  }
+  const int M = p.M, K = p.K;
+  const CUtensorMap& ma = tensor_map_f16(A, uint64_t(M), uint64_t(K), uint64_t(K), BK, BM, 128);
+  const CUtensorMap& mb = tensor_map_f16(W, uint64_t(NF), uint64_t(K), uint64_t(K), BK, G::BQ, 128);
+  const CUtensorMap& mr = tensor_map_f16(R, uint64_t(M), uint64_t(NF), uint64_t(NF), 64, 128, 128);
+  const CUtensorMap& mo = tensor_map_f16(O, uint64_t(M), uint64_t(NF), uint64_t(NF), 64, 128, 128);
+  const int tiles = (M + 2 * BM - 1) / (2 * BM);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * std::min(tiles, max_pairs), 1, 1);
+  cfg.blockDim = dim3(G::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = G::SMEM;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  KH_CUDA(cudaLaunchKernelEx(&cfg, gemm_addln_kernel<NF>, ma, mb, mr, mo, p));
+}
+
+void launch_gemm_addln(const void* A, const void* W, const void* bias, const void* R, const void* ln_w,
+                       const void* ln_b, float eps, void* O, int M, int N, int K, cudaStream_t st) {
+  if (M <= 0) return;
+  if (!gemm_tc_supported_addln(N, K)) throw PlanError("gemm+layernorm: unsupported shape");
+  if (!ln_w) throw PlanError("gemm+layernorm: the norm weight is required");
+  LnParams p;
+  p.M = M;
+  p.K = K;
+  p.bias = static_cast<const __half*>(bias);
+  p.ln_w = static_cast<const __half*>(ln_w);
+  p.ln_b = static_cast<const __half*>(ln_b);
+  p.eps = eps;
+  if (N == 256) launch_addln_nf<256>(A, W, R, O, p, st);
+  else launch_addln_nf<384>(A, W, R, O, p, st);
 }
 
 int tc_error_code() {

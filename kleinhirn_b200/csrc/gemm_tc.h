@@ -33,6 +33,12 @@ DevTensor gemm_geglu_bias(Ctx* ctx, const std::string& name, int N);
 void launch_gemm(Ctx* ctx, bool f16, const void* A, const void* W, const void* bias, void* C, int M, int N, int K,
                  int act, const GemmEpilogue& e, cudaStream_t st);
 
+// O = LayerNorm(R + round(A W^T + bias)) * ln_w + ln_b (a matmul followed by a mode-2 layernorm
+// over its output, f16), for N in {256, 384}. ln_b may be null.
+bool gemm_tc_supported_addln(int N, int K);
+void launch_gemm_addln(const void* A, const void* W, const void* bias, const void* R, const void* ln_w,
+                       const void* ln_b, float eps, void* O, int M, int N, int K, cudaStream_t st);
+
 }  // namespace kh
 
 namespace kh {

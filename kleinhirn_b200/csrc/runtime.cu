@@ -356,6 +356,42 @@ void plan_compile(Ctx* ctx, const Json& plan, CompiledPlan& cp) {
       std::string res_id, out_id = c_id;
       int out_cols = N;
       const std::string wname = bind(op, 1).substr(2);
+      // matmul + layernorm mode 2 over (residual, matmul output): one kernel (post-norm layers)
+      bool addln = false;
+      std::string ln_res, ln_out;
+      Ref ln_w, ln_b;
+      float ln_eps = 0.f;
+      if (f16 && !fixed_rows && act == 0 && i + 1 < ops.size() && gemm_tc_supported_addln(N, K)) {
+        const Json& nx = *ops[i + 1];
+        if (nx["kernel"].as_str() == "layernorm" && cint(nx, "MODE") == 2 && cint(nx, "N") == N &&
+            !seq_level(nx) && bind(nx, 1) == c_id && bind(nx, 0) != c_id) {
+          addln = true;
+          ln_res = bind(nx, 0);
+          ln_out = bind(nx, 5);
+          ln_w = ref(bind(nx, 2));
+          ln_b = ref(bind(nx, 3));
+          ln_eps = float(cnum(nx, "EPS"));
+          use(ln_res);
+          consumed[i + 1] = true;
+          names.push_back(nx["name"].as_str());
+          written(nx);
+        }
+      }
+      if (addln) {
+        protos.push_back({"gemm", names, [=](const CompiledPlan& c) {
+          const int ia = bi(c, a_id), ir = bi(c, ln_res), io = bi(c, ln_out);
+          auto fb = resolve(c, bias);
+          auto fw = resolve(c, ln_w), fnb = resolve(c, ln_b);
+          const bool bias_zero = !bias.weight, lnb_zero = !ln_b.weight;
+          Step s;
+          s.run = [=](Exec& ex, cudaStream_t st) {
+            launch_gemm_addln(ex.buf(ia), W, bias_zero ? nullptr : fb(ex), ex.buf(ir), fw(ex),
+                              lnb_zero ? nullptr : fnb(ex), ln_eps, ex.buf(io), ex.T, N, K, st);
+          };
+          return s;
+        }});
+        continue;
+      }
       if (f16 && !fixed_rows && act == 0 && i + 1 < ops.size() && gemm_tc_supported(N, K)) {
         const Json& nx = *ops[i + 1];
         const std::string nk = nx["kernel"].as_str();

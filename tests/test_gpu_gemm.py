@@ -145,3 +145,32 @@ def test_rope_epilogue(H):
     q[:, : 2 * H, : D // 2] = x * c - y * s
     q[:, : 2 * H, D // 2:] = y * c + x * s
     assert_f16_close(got, f16(q).reshape(-1), "rope")
+
+
+@pytest.mark.parametrize("N,K,M", [(384, 384, 300), (384, 1536, 700), (256, 768, 129)])
+def test_addnorm_epilogue(N, K, M):
+    """matmul followed by layernorm mode 2 over (residual, matmul output):
+    out = LN(R + f16(A W^T + b)) * w + beta (two-pass variance, src/kernels/layernorm.wgsl)."""
+    L = M
+    eps = 1e-5
+    rng = np.random.default_rng(N + K + M)
+    A = (rng.standard_normal((M, K)) * 0.5).astype(np.float16)
+    W = (rng.standard_normal((N, K)) * 0.05).astype(np.float16)
+    b = (rng.standard_normal(N) * 0.1).astype(np.float16)
+    R = rng.standard_normal((M, N)).astype(np.float16)
+    g = (1 + 0.1 * rng.standard_normal(N)).astype(np.float16)
+    beta = (0.1 * rng.standard_normal(N)).astype(np.float16)
+    ops = [{"name": "attnOut", "kernel": "mmtile", "constants": {"M": M, "N": N, "K": K, "ACT": 0},
+            "bind": ["ctx", "w:w", "w:b", "attnOut"], "dispatch": [1, "rows32"]},
+           {"name": "lnA", "kernel": "layernorm", "constants": {"N": N, "MODE": 2, "EPS": eps},
+            "bind": ["x", "attnOut", "w:g", "w:beta", "mask", "tmp"], "dispatch": ["rows", 1]}]
+    plan = f16plan(ops, {"ctx": (M * K, None), "attnOut": (M * N, None), "x": (M * N, None), "tmp": (M * N, None)},
+                   L, "tmp")
+    got, labels = run(plan, {"w": W, "b": b, "g": g, "beta": beta}, {"ctx": A, "x": R}, M, "tmp", M * N)
+    assert labels[0]["label"] == "gemm" and labels[0]["ops"] == ["attnOut", "lnA"]
+    y = f16(A.astype(np.float64) @ W.astype(np.float64).T + b)
+    v = R.astype(np.float64) + y
+    mean = v.mean(axis=1, keepdims=True)
+    var = ((v - mean) ** 2).mean(axis=1, keepdims=True)
+    want = f16((v - mean) / np.sqrt(var + eps) * g.astype(np.float64) + beta.astype(np.float64))
+    assert_f16_close(got, want.reshape(-1), f"add+layernorm N={N} K={K}")
