@@ -133,6 +133,18 @@ int kh_bulk_set_lengths(kh_bulk* bulk, const int32_t* seq_lens, int n);
  * position row in the high 16 bits); type_ids may be null otherwise. Host to device copy. */
 int kh_bulk_upload(kh_bulk* bulk, const void* emb, size_t emb_bytes, const uint32_t* type_ids, size_t type_len);
 
+/* Device-resident word table for bulk runs: tensor `name` (added with kh_add_tensor, shape
+ * [vocab, embeddingSize]) is kept on the device and the rows of packed token ids are gathered
+ * there (kh_bulk_upload_ids), instead of the host gathering word rows (wordRows,
+ * src/encoder.ts:273-314) from the table the reference keeps on the host
+ * (src/wasm-backend.ts:184). Beyond the reference interface. */
+int kh_bulk_set_word_table(kh_bulk* bulk, const char* name);
+
+/* Packed token ids [sum(len)] int32 of the sequences set last, and typeIds as for
+ * kh_bulk_upload (null when the plan has none); the word rows are gathered on the device. An id
+ * outside [0, vocab) gives a zero row, and the next kh_bulk_read returns KH_ERR_ARG. */
+int kh_bulk_upload_ids(kh_bulk* bulk, const int32_t* ids, size_t n, const uint32_t* type_ids, size_t type_len);
+
 /* Device-side forward of every sequence (no host copies; returns when the launches are queued). */
 int kh_bulk_run(kh_bulk* bulk);
 

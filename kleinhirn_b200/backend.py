@@ -51,6 +51,8 @@ _SIGS = {
     "kh_bulk_create": ([_P, ctypes.c_int64, ctypes.c_int, ctypes.c_int64, ctypes.POINTER(_P)], ctypes.c_int),
     "kh_bulk_set_lengths": ([_P, _P, ctypes.c_int], ctypes.c_int),
     "kh_bulk_upload": ([_P, _P, ctypes.c_size_t, _P, ctypes.c_size_t], ctypes.c_int),
+    "kh_bulk_set_word_table": ([_P, ctypes.c_char_p], ctypes.c_int),
+    "kh_bulk_upload_ids": ([_P, _P, ctypes.c_size_t, _P, ctypes.c_size_t], ctypes.c_int),
     "kh_bulk_run": ([_P], ctypes.c_int),
     "kh_bulk_read": ([_P, _P, ctypes.c_size_t], ctypes.c_int),
     "kh_run_batch": ([_P, _P, ctypes.c_int, _P, ctypes.c_size_t, _P, ctypes.c_size_t, _P, ctypes.c_size_t],
@@ -255,6 +257,22 @@ class CudaBulk:
 
     def read_ptr(self, out_ptr: int, n: int) -> None:
         _check(self.lib, self.lib.kh_bulk_read(self.handle, ctypes.c_void_p(out_ptr), n))
+
+    def set_word_table(self, name: str) -> None:
+        """Keep the added tensor `name` ([vocab, embeddingSize]) as the device word table."""
+        _check(self.lib, self.lib.kh_bulk_set_word_table(self.handle, name.encode()))
+
+    def upload_ids(self, ids: np.ndarray, type_ids: np.ndarray | None = None) -> None:
+        """Packed token ids of the sequences set last; word rows are gathered on the device."""
+        i = np.ascontiguousarray(ids, dtype=np.int32)
+        t = None if type_ids is None else np.ascontiguousarray(type_ids, dtype=np.uint32)
+        _check(self.lib, self.lib.kh_bulk_upload_ids(self.handle, _ptr(i), i.size, _ptr(t), 0 if t is None else t.size))
+
+    def upload_ids_ptr(self, ids_ptr: int, n: int, type_ptr: int | None, type_len: int) -> None:
+        """upload_ids from raw host pointers (pinned buffers of the caller)."""
+        _check(self.lib, self.lib.kh_bulk_upload_ids(self.handle, ctypes.c_void_p(ids_ptr), n,
+                                                     None if type_ptr is None else ctypes.c_void_p(type_ptr),
+                                                     type_len))
 
     def last_timing(self) -> tuple[float, int]:
         ms, n = ctypes.c_float(), ctypes.c_int64()

@@ -48,6 +48,10 @@ struct kh_bulk {
   int64_t n_tokens = 0;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   int64_t last_launches = 0;
+  const void* d_words = nullptr;  // device word table (kh_bulk_set_word_table)
+  int64_t vocab = 0;
+  int32_t* d_ids = nullptr;       // packed token ids of kh_bulk_upload_ids
+  bool ids_used = false;          // the last upload gathered rows on the device
   ~kh_bulk();
 };
 
@@ -132,6 +136,7 @@ kh_bulk::~kh_bulk() {
   cudaFree(d_mask);
   cudaFree(d_out);
   cudaFree(d_table);
+  cudaFree(d_ids);
   if (ev0) cudaEventDestroy(ev0);
   if (ev1) cudaEventDestroy(ev1);
 }
@@ -555,6 +560,48 @@ int kh_bulk_upload(kh_bulk* bulk, const void* emb, size_t emb_bytes, const uint3
   });
 }
 
+int kh_bulk_set_word_table(kh_bulk* bulk, const char* name) {
+  if (!bulk || !name) {
+    g_err = "kh_bulk_set_word_table: bulk and name are required";
+    return KH_ERR_ARG;
+  }
+  Ctx* c = bulk->plan->owner->c.get();
+  return guard(c, Latch::No, [&] {
+    const kh::CompiledPlan& cp = bulk->plan->cp;
+    if (!c->tensors.count(name)) throw kh::ArgError(std::string("kh_bulk_set_word_table: no tensor ") + name);
+    const kh::DevTensor& t = c->weight(name, cp.f16);
+    if (t.shape.size() != 2 || t.shape[1] != cp.emb_size)
+      throw kh::ArgError(std::string("kh_bulk_set_word_table: ") + name + " is not [vocab, " +
+                         std::to_string(cp.emb_size) + "]");
+    if (!bulk->d_ids) KH_CUDA(cudaMalloc((void**)&bulk->d_ids, size_t(bulk->max_tokens) * 4 + 256));
+    bulk->d_words = t.ptr;
+    bulk->vocab = t.shape[0];
+  });
+}
+
+int kh_bulk_upload_ids(kh_bulk* bulk, const int32_t* ids, size_t n, const uint32_t* type_ids, size_t type_len) {
+  if (!bulk || !ids) {
+    g_err = "kh_bulk_upload_ids: bulk and ids are required";
+    return KH_ERR_ARG;
+  }
+  Ctx* c = bulk->plan->owner->c.get();
+  return guard(c, Latch::Yes, [&] {
+    const kh::CompiledPlan& cp = bulk->plan->cp;
+    if (!bulk->d_words) throw kh::ArgError("kh_bulk_upload_ids: no word table (kh_bulk_set_word_table)");
+    if (n != size_t(bulk->n_tokens))
+      throw kh::ArgError("kh_bulk_upload_ids: " + std::to_string(n) + " ids, the sequences have " +
+                         std::to_string(bulk->n_tokens) + " rows");
+    KH_CUDA(cudaMemcpyAsync(bulk->d_ids, ids, n * 4, cudaMemcpyHostToDevice, c->stream));
+    if (!cp.in_type.empty()) {
+      if (!type_ids || type_len != size_t(bulk->n_tokens)) throw kh::ArgError("plan needs typeIds for every row");
+      KH_CUDA(cudaMemcpyAsync(bulk->d_type, type_ids, type_len * 4, cudaMemcpyHostToDevice, c->stream));
+    }
+    kh::launch_gather_rows(cp.f16, bulk->d_words, bulk->vocab, bulk->d_ids, int64_t(n), cp.emb_size, bulk->d_emb,
+                           c->stream);
+    bulk->ids_used = true;
+  });
+}
+
 int kh_bulk_run(kh_bulk* bulk) {
   if (!bulk) {
     g_err = "kh_bulk_run: null bulk";
@@ -604,6 +651,13 @@ int kh_bulk_read(kh_bulk* bulk, float* out, size_t n) {
     KH_CUDA(cudaMemcpyAsync(out, bulk->d_out, need * 4, cudaMemcpyDeviceToHost, c->stream));
     KH_CUDA(cudaStreamSynchronize(c->stream));
     check_pipelines();
+    if (bulk->ids_used) {
+      bulk->ids_used = false;
+      const int bad = kh::gather_error_code();
+      if (bad)
+        throw kh::ArgError("kh_bulk_read: " + std::to_string(bad) +
+                           " token ids outside the word table (their rows were zeros)");
+    }
   });
 }
 

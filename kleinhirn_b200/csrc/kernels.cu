@@ -7,6 +7,7 @@
 // (v - mean)^2, src/kernels/layernorm.wgsl:18-20).
 
 #include "kernels.h"
+#include "runtime.h"
 
 #include <cmath>
 #include <cstdio>
@@ -677,6 +678,45 @@ void launch_f32_to_f16(const float* src, __half* dst, int64_t n, cudaStream_t st
 }
 void launch_f16_to_f32(const __half* src, float* dst, int64_t n, cudaStream_t st) {
   if (n > 0) f16_to_f32_kernel<<<grid_for(n, 256), 256, 0, st>>>(src, dst, n);
+}
+
+namespace {
+__device__ int kh_gather_bad = 0;
+
+// One warp per row, 16-byte copies (E * element size is a multiple of 16 bytes).
+__global__ void gather_rows_kernel(const uint4* __restrict__ table, int64_t vocab, const int32_t* __restrict__ ids,
+                                   int64_t n, int row_vecs, uint4* __restrict__ out) {
+  const int64_t row = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= n) return;
+  const int32_t id = ids[row];
+  const bool ok = id >= 0 && int64_t(id) < vocab;
+  if (!ok && lane == 0) atomicAdd(&kh_gather_bad, 1);
+  const uint4* src = table + int64_t(ok ? id : 0) * row_vecs;
+  uint4* dst = out + row * row_vecs;
+  for (int v = lane; v < row_vecs; v += 32) dst[v] = ok ? __ldg(src + v) : make_uint4(0, 0, 0, 0);
+}
+}  // namespace
+
+void launch_gather_rows(bool f16, const void* table, int64_t vocab, const int32_t* ids, int64_t n, int E, void* out,
+                        cudaStream_t st) {
+  if (n <= 0) return;
+  const int64_t row_bytes = int64_t(E) * (f16 ? 2 : 4);
+  if (row_bytes % 16) throw PlanError("word rows must be a multiple of 16 bytes");
+  const int64_t threads = n * 32;
+  gather_rows_kernel<<<unsigned((threads + 255) / 256), 256, 0, st>>>(
+      static_cast<const uint4*>(table), vocab, ids, n, int(row_bytes / 16), static_cast<uint4*>(out));
+  KH_CUDA(cudaGetLastError());
+}
+
+int gather_error_code() {
+  int v = 0;
+  KH_CUDA(cudaMemcpyFromSymbol(&v, kh_gather_bad, sizeof(int)));
+  if (v) {
+    const int zero = 0;
+    KH_CUDA(cudaMemcpyToSymbol(kh_gather_bad, &zero, sizeof(int)));
+  }
+  return v;
 }
 
 }  // namespace kh

@@ -91,4 +91,12 @@ void launch_attention_simt(bool f16, const AttnArgs& a, const SeqTable& seq, cud
 void launch_f32_to_f16(const float* src, __half* dst, int64_t n, cudaStream_t st);
 void launch_f16_to_f32(const __half* src, float* dst, int64_t n, cudaStream_t st);
 
+// out[i] = table[ids[i]] for n rows of E elements (f16 or f32): the word rows of packed token ids
+// (wordRows, src/encoder.ts:273-314) gathered on the device. An id outside [0, vocab) writes a
+// zero row and records the failure for gather_error_code().
+void launch_gather_rows(bool f16, const void* table, int64_t vocab, const int32_t* ids, int64_t n, int E, void* out,
+                        cudaStream_t st);
+// Number of out-of-range ids seen since the last call (0: none); resets the count. Syncs.
+int gather_error_code();
+
 }  // namespace kh

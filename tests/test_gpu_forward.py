@@ -113,3 +113,37 @@ def test_batch_plan_matches_single_calls(backend_factory):
     ragged = enc.run_ragged(id_lists)
     assert np.allclose(batched, single, atol=1e-3), np.abs(batched - single).max()
     assert np.allclose(ragged, single, atol=2e-3), np.abs(ragged - single).max()
+
+
+def test_bulk_ids_gathered_on_device(backend_factory):
+    """kh_bulk_upload_ids with the word table on the device gives the bits of kh_bulk_upload with
+    host-gathered word rows; an id outside the table is reported by the next read."""
+    from kleinhirn_b200.backend import KhError
+    from kleinhirn_b200.encoder import packed_inputs
+    from kleinhirn_b200.plan import build_plan
+    m, ids = baseline_case("mminilm-l12-xlmr", 2, [142, 36, 300, 7], 512)
+    be = backend_factory(m)
+    be.add_tensor("embeddings.word.weight", m.word_table)
+    plan = build_plan(m.spec, m.head, 512, 1, 0, m.f16)
+    r = be.runner(plan)
+    emb, types, lens = packed_inputs(m.spec, m.word_table, [np.asarray(x) for x in ids])
+    flat = np.concatenate([np.asarray(x, dtype=np.int32) for x in ids])
+    tt = types if "typeIds" in plan["inputs"] else None
+    bulk = be.bulk(r, int(lens.sum()), len(lens), 600)
+    want = bulk.run_batch(lens, emb, tt)
+    bulk.set_word_table("embeddings.word.weight")
+    for _ in range(2):
+        bulk.set_lengths(lens)
+        bulk.upload_ids(flat, tt)
+        bulk.run()
+        got = bulk.read()
+        assert np.array_equal(got, want)
+    bad = flat.copy()
+    bad[5] = m.spec["vocab"]
+    bulk.set_lengths(lens)
+    bulk.upload_ids(bad, tt)
+    bulk.run()
+    with pytest.raises(KhError, match="outside the word table"):
+        bulk.read()
+    bulk.close()
+    r.destroy()
