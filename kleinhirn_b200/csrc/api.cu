@@ -501,40 +501,61 @@ int kh_bulk_set_lengths(kh_bulk* bulk, const int32_t* seq_lens, int n) {
     if (total > bulk->max_tokens)
       throw kh::ArgError("kh_bulk_set_lengths: " + std::to_string(total) + " rows, room for " +
                          std::to_string(bulk->max_tokens));
+    // chunks on the host (O(sequences)); their tables are built on the device
     bulk->chunks.clear();
-    std::vector<int32_t> all;
+    std::vector<kh::ChunkDesc> descs;
     int s = 0;
-    int64_t tok = 0;
-    const int cap_seqs = bulk->ex.cap_seqs;
+    int64_t tok = 0, words = 0;
+    const int cap_seqs = std::min(bulk->ex.cap_seqs, 1024 * 64);
     while (s < n) {
       kh_bulk::Chunk ch;
       ch.seq0 = s;
       ch.tok0 = tok;
-      std::vector<int32_t> lens;
       int64_t T = 0;
-      while (s < n && T + seq_lens[s] <= bulk->chunk_tokens && int(lens.size()) < cap_seqs) {
-        lens.push_back(seq_lens[s]);
+      int S = 0, ntiles = 0, max_len = 0;
+      while (s < n && T + seq_lens[s] <= bulk->chunk_tokens && S < cap_seqs) {
         T += seq_lens[s];
+        ntiles += (seq_lens[s] + cp.tile_q - 1) / cp.tile_q;
+        max_len = std::max(max_len, int(seq_lens[s]));
+        ++S;
         ++s;
       }
-      std::vector<int32_t> table;
-      int64_t t2 = 0;
-      kh::build_seq_table(lens, cp.tile_q, table, ch.seq, t2);
+      const int nptiles = int((T + kh::PACKED_TILE - 1) / kh::PACKED_TILE);
       ch.T = T;
-      ch.S = int(lens.size());
-      ch.word0 = int64_t(all.size());
-      all.insert(all.end(), table.begin(), table.end());
+      ch.S = S;
+      ch.word0 = words;
+      kh::SeqTable& o = ch.seq;  // word offsets, rebased on d_table at run time
+      o.start = (const int32_t*)(intptr_t)0;
+      o.len = (const int32_t*)(intptr_t)S;
+      o.row_pos = (const int32_t*)(intptr_t)(2 * S);
+      o.row_seq = (const int32_t*)(intptr_t)(2 * S + T);
+      o.tiles = (const int32_t*)(intptr_t)(2 * S + 2 * T);
+      o.ptiles = (const int32_t*)(intptr_t)(2 * S + 2 * T + 2 * ntiles);
+      o.count = S;
+      o.max_len = max_len;
+      o.ntiles = ntiles;
+      o.nptiles = nptiles;
+      descs.push_back({tok, words, ch.seq0, S, int32_t(T), ntiles});
+      words += 2 * int64_t(S) + 2 * T + 2 * int64_t(ntiles) + 3 * int64_t(nptiles);
       bulk->chunks.push_back(ch);
       tok += T;
     }
-    const int64_t words = int64_t(all.size());
-    if (words > bulk->table_cap) {
+    // device room: the tables, the lengths and the chunk descriptors (grown, never shrunk)
+    const int64_t desc_words = int64_t(descs.size() * sizeof(kh::ChunkDesc) + 3) / 4;
+    const int64_t need = words + n + desc_words + 64;
+    if (need > bulk->table_cap) {
       cudaFree(bulk->d_table);
       bulk->d_table = nullptr;
-      KH_CUDA(cudaMalloc((void**)&bulk->d_table, size_t(words) * 4));
-      bulk->table_cap = words;
+      KH_CUDA(cudaMalloc((void**)&bulk->d_table, size_t(need) * 4));
+      bulk->table_cap = need;
     }
-    KH_CUDA(cudaMemcpy(bulk->d_table, all.data(), size_t(words) * 4, cudaMemcpyHostToDevice));
+    int32_t* d_lens = bulk->d_table + words;
+    kh::ChunkDesc* d_descs = reinterpret_cast<kh::ChunkDesc*>(bulk->d_table + ((words + n + 3) & ~int64_t(3)));
+    KH_CUDA(cudaMemcpyAsync(d_lens, seq_lens, size_t(n) * 4, cudaMemcpyHostToDevice, c->stream));
+    KH_CUDA(cudaMemcpyAsync(d_descs, descs.data(), descs.size() * sizeof(kh::ChunkDesc), cudaMemcpyHostToDevice,
+                            c->stream));
+    // (copies from pageable host memory have read the host arrays when they return)
+    kh::launch_build_seq_tables(d_lens, d_descs, int(descs.size()), total, cp.tile_q, bulk->d_table, c->stream);
     bulk->n_seqs = n;
     bulk->n_tokens = total;
   });

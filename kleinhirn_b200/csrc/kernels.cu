@@ -719,4 +719,99 @@ int gather_error_code() {
   return v;
 }
 
+namespace {
+// One CTA per chunk: sequence starts and lengths, and the attention work tiles (seq, q0), from an
+// exclusive scan of the lengths and of the tiles per sequence.
+__global__ void seqtable_chunk_kernel(const int32_t* __restrict__ lens, const ChunkDesc* __restrict__ chunks,
+                                      int tile_q, int32_t* __restrict__ table) {
+  __shared__ int32_t part_len[1024], part_tiles[1024];
+  const ChunkDesc c = chunks[blockIdx.x];
+  int32_t* start = table + c.word0;
+  int32_t* len = start + c.S;
+  int32_t* tiles = len + c.S + 2 * int64_t(c.T);
+  const int per = (c.S + blockDim.x - 1) / blockDim.x;
+  const int b0 = threadIdx.x * per;
+  int32_t sl = 0, st = 0;
+  for (int i = 0; i < per; ++i)
+    if (b0 + i < c.S) {
+      const int32_t l = lens[c.seq0 + b0 + i];
+      sl += l;
+      st += (l + tile_q - 1) / tile_q;
+    }
+  part_len[threadIdx.x] = sl;
+  part_tiles[threadIdx.x] = st;
+  __syncthreads();
+  for (int off = 1; off < int(blockDim.x); off <<= 1) {
+    const int32_t a = int(threadIdx.x) >= off ? part_len[threadIdx.x - off] : 0;
+    const int32_t b = int(threadIdx.x) >= off ? part_tiles[threadIdx.x - off] : 0;
+    __syncthreads();
+    part_len[threadIdx.x] += a;
+    part_tiles[threadIdx.x] += b;
+    __syncthreads();
+  }
+  int32_t rl = part_len[threadIdx.x] - sl, rt = part_tiles[threadIdx.x] - st;
+  for (int i = 0; i < per; ++i)
+    if (b0 + i < c.S) {
+      const int s = b0 + i;
+      const int32_t l = lens[c.seq0 + s];
+      start[s] = rl;
+      len[s] = l;
+      for (int q = 0; q < l; q += tile_q) {
+        tiles[2 * rt] = s;
+        tiles[2 * rt + 1] = q;
+        ++rt;
+      }
+      rl += l;
+    }
+}
+
+// Thread per packed row of the whole bulk: its chunk, sequence and local position, and for the
+// first row of every 128-row tile the tile's key range.
+__global__ void seqtable_rows_kernel(const ChunkDesc* __restrict__ chunks, int n_chunks, int64_t total_rows,
+                                     int32_t* __restrict__ table) {
+  const int64_t g = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (g >= total_rows) return;
+  int lo = 0, hi = n_chunks - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (chunks[mid].tok0 <= g) lo = mid;
+    else hi = mid - 1;
+  }
+  const ChunkDesc c = chunks[lo];
+  const int r = int(g - c.tok0);
+  const int32_t* start = table + c.word0;
+  const int32_t* len = start + c.S;
+  int32_t* pos = table + c.word0 + 2 * int64_t(c.S);
+  int32_t* rseq = pos + c.T;
+  int32_t* ptiles = rseq + c.T + 2 * int64_t(c.ntiles);
+  auto seq_of = [&](int row) {
+    int a = 0, b = c.S - 1;  // lengths >= 1: starts strictly increase
+    while (a < b) {
+      const int mid = (a + b + 1) >> 1;
+      if (start[mid] <= row) a = mid;
+      else b = mid - 1;
+    }
+    return a;
+  };
+  const int s = seq_of(r);
+  pos[r] = r - start[s];
+  rseq[r] = s;
+  if (r % PACKED_TILE == 0) {
+    const int s1 = seq_of(min(c.T, r + PACKED_TILE) - 1);
+    int32_t* pt = ptiles + 3 * (r / PACKED_TILE);
+    pt[0] = r;
+    pt[1] = start[s];
+    pt[2] = start[s1] + len[s1];
+  }
+}
+}  // namespace
+
+void launch_build_seq_tables(const int32_t* lens, const ChunkDesc* chunks, int n_chunks, int64_t total_rows,
+                             int tile_q, int32_t* table, cudaStream_t st) {
+  if (n_chunks <= 0 || total_rows <= 0) return;
+  seqtable_chunk_kernel<<<n_chunks, 1024, 0, st>>>(lens, chunks, tile_q, table);
+  seqtable_rows_kernel<<<unsigned((total_rows + 255) / 256), 256, 0, st>>>(chunks, n_chunks, total_rows, table);
+  KH_CUDA(cudaGetLastError());
+}
+
 }  // namespace kh

@@ -99,4 +99,15 @@ void launch_gather_rows(bool f16, const void* table, int64_t vocab, const int32_
 // Number of out-of-range ids seen since the last call (0: none); resets the count. Syncs.
 int gather_error_code();
 
+// Sequence tables of a bulk run's chunks, built on the device from the sequence lengths. Chunk c
+// covers sequences [seq0, seq0 + S) and packed rows [tok0, tok0 + T); its table starts at word
+// word0 of `table` in the build_seq_table layout: start[S], len[S], row_pos[T], row_seq[T],
+// tiles[2 ntiles] (attention work tiles of tile_q rows), ptiles[3 ceil(T / 128)].
+struct ChunkDesc {
+  int64_t tok0, word0;
+  int32_t seq0, S, T, ntiles;
+};
+void launch_build_seq_tables(const int32_t* lens, const ChunkDesc* chunks, int n_chunks, int64_t total_rows,
+                             int tile_q, int32_t* table, cudaStream_t st);
+
 }  // namespace kh
