@@ -212,7 +212,7 @@ def run_reference(args):
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 1000.0 * args.pairs / value, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": f"{WORKLOAD} 65536-pair rerank (BASELINE config 5)", "pairs": args.pairs,
+            "config": {"workload": f"{WORKLOAD} {args.pairs}-pair rerank (BASELINE config 5)", "pairs": args.pairs,
                        "bucket": BUCKET},
             "cpu_baseline": {"value": value, "unit": "pairs/s", "cores": threads, "kind": "port",
                              "sample": res["sample"] if res else ""},
@@ -232,7 +232,7 @@ def main():
     if world > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=torch.device("cuda", local))
     from kleinhirn_b200 import synthetic
     from kleinhirn_b200.backend import CudaBackend

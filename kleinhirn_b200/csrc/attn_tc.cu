@@ -63,7 +63,11 @@ struct Cfg {
   static constexpr int P_OFF = V_OFF + VS * TILE;  // 2 blocks of 128 rows x 64 keys, 16 KB each
   static constexpr int BITS_OFF = P_OFF + 32768;   // present-and-unmasked / masked-key bits
   static constexpr int XCH_OFF = BITS_OFF + 2 * MAXKT * 4 * 4;  // row max / sum exchange of the two halves
-  static constexpr int BAR_OFF = XCH_OFF + 2 * (4 * 2 * 2 * 128);  // xmax and xsum, f32 [2][2][128] each
+  // D = 32: the row sums come from the tensor core (P times a ones tile, 16 columns of TMEM per
+  // head parity next to O); D = 64 has no TMEM room left and sums in the softmax threads.
+  static constexpr bool SUMS = D == 32;
+  static constexpr int ONES_OFF = XCH_OFF + 2 * (4 * 2 * 2 * 128);  // xmax and xsum, f32 [2][2][128] each
+  static constexpr int BAR_OFF = ONES_OFF + (SUMS ? 4096 : 0);       // ones: 2 blocks of 16 rows x 64 keys
   static constexpr int USED = BAR_OFF + 256;
   // at least 100 KB so that no more than two CTAs (2 x 256 TMEM columns) share an SM
   static constexpr int SMEM = (USED + 1024 > 102400 ? USED + 1024 : 102400);
@@ -146,6 +150,12 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
     fence_barrier_init();
     prefetch_tmap(&tm);
   }
+  if constexpr (C::SUMS) {
+    // B operand of the row-sum MMA: 16 x 128 f16 ones (every swizzle of it is the same)
+    uint4* ones = reinterpret_cast<uint4*>(smem + C::ONES_OFF);
+    for (int i = threadIdx.x; i < 4096 / 16; i += THREADS) ones[i] = make_uint4(0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);
+    fence_proxy_async_smem();
+  }
   if (warp == 1) tmem_alloc(tmem_holder, TMEM_COLS);
   fence_before_sync();
   __syncthreads();
@@ -157,8 +167,10 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
       bool ok = true;
       // issued loads not yet known complete: parity per ring slot (bit 2 = issued)
       uint32_t pend_q = 0, pend_k = 0, pend_v = 0;
-      for (int it = 0; it < NI && ok; ++it) {
-        const int hh = it / nkt, j = it - hh * nkt, h = hg0 + hh;
+      // (head, key tile) of item it, advanced without a division
+      int hh = 0, j = 0;
+      for (int it = 0; it < NI && ok; ++it, j = (j + 1 == nkt) ? (++hh, 0) : j + 1) {
+        const int h = hg0 + hh;
         const int y = kstart + j * TKEYS;
         if (j == 0) {
           const int s = hh % C::QS;
@@ -200,8 +212,10 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
       const uint32_t idesc_s = idesc_f16(128, TKEYS);
       const uint32_t idesc_o = idesc_f16(128, D) | (1u << 16);  // B (V) MN-major
       bool ok = true;
+      int sh = 0, sj = 0;  // (head, key tile) of the next S to issue
       auto issue_s = [&](int it) -> bool {
-        const int hh = it / nkt, j = it - hh * nkt;
+        const int hh = sh, j = sj;
+        sj = (sj + 1 == nkt) ? (++sh, 0) : sj + 1;
         const int qs = hh % C::QS, ks = it % C::KS;
         if (j == 0 && !mbar_wait(&q_full[qs], uint32_t(hh / C::QS) & 1, 23)) return false;
         if (*abort_flag || !mbar_wait(&k_full[ks], uint32_t(it / C::KS) & 1, 24)) return false;
@@ -217,9 +231,9 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
         return true;
       };
       ok = NI > 0 && issue_s(0);
-      for (int it = 0; it < NI && ok; ++it) {
+      int hh = 0, j = 0;  // (head, key tile) of the PV product of item it
+      for (int it = 0; it < NI && ok; ++it, j = (j + 1 == nkt) ? (++hh, 0) : j + 1) {
         if (it + 1 < NI && !issue_s(it + 1)) { ok = false; break; }
-        const int hh = it / nkt, j = it - hh * nkt;
         const int vs = it % C::VS;
         if (*abort_flag || !mbar_wait(p_full, uint32_t(it & 1), 26) ||
             !mbar_wait(&v_full[vs], uint32_t(it / C::VS) & 1, 27)) {
@@ -234,6 +248,17 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
         for (int kk = 0; kk < TKEYS / 16; ++kk) {
           const uint64_t dp = desc_rows<64>(sP + (kk >> 2) * 16384) + uint64_t(2 * (kk & 3));
           mma_f16(o_addr, dp, dv + uint64_t(2 * D * kk), idesc_o, (j | kk) ? 1u : 0u);
+        }
+        if constexpr (C::SUMS) {
+          // row sums of P: P times the ones tile, accumulated like O
+          const uint32_t l_addr = tmem + 192 + uint32_t((hh & 1) * 16);
+          const uint32_t idesc_l = idesc_f16(128, 16);
+#pragma unroll
+          for (int kk = 0; kk < TKEYS / 16; ++kk) {
+            const uint64_t dp = desc_rows<64>(sP + (kk >> 2) * 16384) + uint64_t(2 * (kk & 3));
+            const uint64_t d1 = desc_rows<64>(smem + C::ONES_OFF + (kk >> 2) * 2048) + uint64_t(2 * (kk & 3));
+            mma_f16(l_addr, dp, d1, idesc_l, (j | kk) ? 1u : 0u);
+          }
         }
         mma_commit(o_full);
         mma_commit(&v_empty[vs]);
@@ -311,9 +336,17 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
     // context row of head hh = O / l over this thread's D / 2 columns (a masked query row, or
     // one without a kept key, is exactly zero: select, not multiply)
     auto finish_head = [&](int hh) {
-      xsum[((hh & 1) * 2 + hf) * 128 + r_local] = l;
-      named_bar(pair_bar, 64);
-      const float lt = l + xsum[((hh & 1) * 2 + (hf ^ 1)) * 128 + r_local];
+      float lt;
+      if constexpr (C::SUMS) {
+        uint32_t lr[8];
+        tmem_ld8(trow + 192 + uint32_t((hh & 1) * 16), lr);
+        tmem_ld_wait();
+        lt = __uint_as_float(lr[0]);
+      } else {
+        xsum[((hh & 1) * 2 + hf) * 128 + r_local] = l;
+        named_bar(pair_bar, 64);
+        lt = l + xsum[((hh & 1) * 2 + (hf ^ 1)) * 128 + r_local];
+      }
       const bool live = qvalid && lt > 0.f;
       const float inv = live ? 1.0f / lt : 0.f;
       const uint32_t o_addr = trow + 128 + uint32_t((hh & 1) * D + hf * (D / 2));
@@ -331,8 +364,8 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
         if (in_range) dst[c / 8] = *reinterpret_cast<uint4*>(hv);
       }
     };
-    for (int it = 0; it < NI; ++it) {
-      const int hh = it / nkt, j = it - hh * nkt;
+    int hh = 0, j = 0;  // (head, key tile) of item it
+    for (int it = 0; it < NI; ++it, j = (j + 1 == nkt) ? (++hh, 0) : j + 1) {
       // A failed wait never ends one warp of a pair alone: the pair decides together at its
       // named barriers (bar.red), so neither warp is left waiting at one.
       bool fail = !ok;
@@ -419,6 +452,17 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
           for (int e = 0; e < 8; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * corr);
           tmem_st8(o_addr + c, r);
         }
+        if constexpr (C::SUMS) {
+          if (hf == 0) {  // the row-sum columns, once per row
+            const uint32_t l_addr = trow + 192 + uint32_t((hh & 1) * 16);
+            uint32_t r[8];
+            tmem_ld8(l_addr, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 8; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * corr);
+            tmem_st8(l_addr, r);
+          }
+        }
         tmem_st_wait();
         l *= corr;
       }
@@ -439,8 +483,10 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
               const int i = 8 * q + 2 * e2;
               const float x0 = ex2_approx(fmaf(__uint_as_float(sr[32 * c + i]), p.scale_log2, -m));
               const float x1 = ex2_approx(fmaf(__uint_as_float(sr[32 * c + i + 1]), p.scale_log2, -m));
-              ls[i & 3] += x0;
-              ls[(i + 1) & 3] += x1;
+              if constexpr (!C::SUMS) {
+                ls[i & 3] += x0;
+                ls[(i + 1) & 3] += x1;
+              }
               __half2 hv = __floats2half2_rn(x0, x1);
               pk[e2] = *reinterpret_cast<uint32_t*>(&hv);
             }
@@ -453,7 +499,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
                 const int i = 8 * q + 2 * e2 + e;
                 const float x = ex2_approx(fmaf(__uint_as_float(sr[32 * c + i]), p.scale_log2, -m));
                 pv[e] = ((k >> i) & 1u) ? x : 0.f;
-                ls[i & 3] += pv[e];
+                if constexpr (!C::SUMS) ls[i & 3] += pv[e];
               }
               __half2 hv = __floats2half2_rn(pv[0], pv[1]);
               pk[e2] = *reinterpret_cast<uint32_t*>(&hv);

@@ -459,7 +459,8 @@ struct LCfg {
   static constexpr int STAGES = NF == 256 ? 4 : 3;
   static constexpr int THREADS = 64 + 512;
   static constexpr int RED_BYTES = 2 * 4 * 128 * 4;  // partial row sums [pass][quarter][row]
-  static constexpr int SMEM = STAGES * STAGE_BYTES + X_BYTES + RED_BYTES + 1024 + 256;
+  static constexpr int VEC_BYTES = 3 * NF * 4;        // bias, ln_w, ln_b as f32
+  static constexpr int SMEM = STAGES * STAGE_BYTES + X_BYTES + RED_BYTES + VEC_BYTES + 1024 + 256;
   static constexpr int D1 = 256;                    // TMEM column of the second MMA's accumulator
 };
 
@@ -484,7 +485,10 @@ __global__ void __launch_bounds__(LCfg<NF>::THREADS, 1)
   uint8_t* sB = smem + STAGES * A_BYTES;
   uint8_t* sX = sB + STAGES * G::B_BYTES;  // [box][128 rows][128 bytes], 128-byte swizzle
   float* red = reinterpret_cast<float*>(sX + G::X_BYTES);
-  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(red) + G::RED_BYTES);
+  float* vbias = red + G::RED_BYTES / 4;  // [NF] matmul bias, then [NF] ln_w, [NF] ln_b, as f32
+  float* vw = vbias + NF;
+  float* vb = vw + NF;
+  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(red) + G::RED_BYTES + G::VEC_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 1;
@@ -608,6 +612,11 @@ __global__ void __launch_bounds__(LCfg<NF>::THREADS, 1)
     const uint32_t trow = tmem + (uint32_t(q * 32) << 16);
     float* red1 = red;            // [quarter][row]: sums
     float* red2 = red + 4 * 128;  // [quarter][row]: squared deviations
+    for (int i = threadIdx.x - 64; i < NF; i += 512) {  // seen by all after the first named barrier
+      vbias[i] = p.bias ? __half2float(p.bias[i]) : 0.f;
+      vw[i] = __half2float(p.ln_w[i]);
+      vb[i] = p.ln_b ? __half2float(p.ln_b[i]) : 0.f;
+    }
     bool res_pending = false;
     int local = 0;
     auto tcol = [&](int c0) { return trow + uint32_t(c0 < G::NH ? c0 : c0 - G::NH + G::D1); };
@@ -616,9 +625,15 @@ __global__ void __launch_bounds__(LCfg<NF>::THREADS, 1)
       uint32_t a[32];
       tmem_ld32(tcol(c0), a);
       tmem_ld_wait();
+      const float4* bs = reinterpret_cast<const float4*>(vbias + c0);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(a[i]);
-      bias_act32<0>(v, p.bias, c0);
+      for (int i4 = 0; i4 < 8; ++i4) {
+        const float4 b4 = bs[i4];
+        v[4 * i4] = __uint_as_float(a[4 * i4]) + b4.x;
+        v[4 * i4 + 1] = __uint_as_float(a[4 * i4 + 1]) + b4.y;
+        v[4 * i4 + 2] = __uint_as_float(a[4 * i4 + 2]) + b4.z;
+        v[4 * i4 + 3] = __uint_as_float(a[4 * i4 + 3]) + b4.w;
+      }
       const uint8_t* xrow = sX + (c0 >> 6) * OUT_BYTES + r * 128;
       const int ch0 = (c0 & 63) >> 3;
 #pragma unroll
@@ -694,23 +709,20 @@ __global__ void __launch_bounds__(LCfg<NF>::THREADS, 1)
         const int c0 = g * QC + cc * 32;
         float v[32];
         load_v(c0, v);
-        const uint4* wv = reinterpret_cast<const uint4*>(p.ln_w + c0);
-        const uint4* bv = reinterpret_cast<const uint4*>(p.ln_b + c0);
         uint8_t* xrow = sX + (c0 >> 6) * OUT_BYTES + r * 128;
         const int ch0 = (c0 & 63) >> 3;
 #pragma unroll
         for (int cq = 0; cq < 4; ++cq) {
-          const uint4 wu = __ldg(wv + cq);
-          const uint4 bu = p.ln_b ? __ldg(bv + cq) : make_uint4(0, 0, 0, 0);
-          const __half2* wh = reinterpret_cast<const __half2*>(&wu);
-          const __half2* bh = reinterpret_cast<const __half2*>(&bu);
+          const float4* w4 = reinterpret_cast<const float4*>(vw + c0 + cq * 8);
+          const float4* b4 = reinterpret_cast<const float4*>(vb + c0 + cq * 8);
+          const float4 wa = w4[0], wb = w4[1], ba = b4[0], bb = b4[1];
+          const float wf[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+          const float bf[8] = {ba.x, ba.y, ba.z, ba.w, bb.x, bb.y, bb.z, bb.w};
           __half2 o[4];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 wf = __half22float2(wh[e]), bf = __half22float2(bh[e]);
-            o[e] = __floats2half2_rn((v[cq * 8 + 2 * e] - mean) * inv * wf.x + bf.x,
-                                     (v[cq * 8 + 2 * e + 1] - mean) * inv * wf.y + bf.y);
-          }
+          for (int e = 0; e < 4; ++e)
+            o[e] = __floats2half2_rn((v[cq * 8 + 2 * e] - mean) * inv * wf[2 * e] + bf[2 * e],
+                                     (v[cq * 8 + 2 * e + 1] - mean) * inv * wf[2 * e + 1] + bf[2 * e + 1]);
           *reinterpret_cast<uint4*>(xrow + (((ch0 + cq) ^ (r & 7)) * 16)) = *reinterpret_cast<uint4*>(o);
         }
       }
