@@ -37,6 +37,13 @@ WORKLOAD = "mminilm-l12-xlmr"
 BUCKET = 512
 
 
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one GEMM launch on a 262,144-row
+# chunk, mean of the four GEMM launches of a layer (qkv 0.750 GB, FFN-in 0.953 GB, attnOut +
+# LayerNorm 0.568 GB, FFN-out + LayerNorm 1.194 GB), from one ncu capture each.
+GEMM_TRAFFIC_BYTES = 866.2e6
+GEMM_TRAFFIC_SOURCE = "ncu, profiles/gemm_pair_c5.md and profiles/gemm_addln_c5.md"
+
+
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -364,7 +371,9 @@ def main():
                     "d2h_bytes_per_step": int(d2h) * world},
             "roofline": {"bound": "tensor", "kernel": "gemm", "achieved": achieved, "peak": peaks["tflops"],
                          "unit": "TFLOP/s", "frac": achieved / peaks["tflops"] if peaks["tflops"] else None,
-                         "peak_source": peaks["source"] + " bf16_tflops_sustained", "traffic": None,
+                         "peak_source": peaks["source"] + " bf16_tflops_sustained",
+                         "traffic": GEMM_TRAFFIC_BYTES, "traffic_unit": "bytes per launch",
+                         "traffic_source": GEMM_TRAFFIC_SOURCE,
                          "share_of_forward": gemm_ms / total_prof if total_prof else None},
             "clocks": clocks.summary(),
         }
