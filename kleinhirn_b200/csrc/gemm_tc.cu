@@ -155,7 +155,7 @@ struct PCfg {
   static constexpr int NWG = BN / 64;
   static constexpr int THREADS = 64 + 128 * NWG;
   static constexpr int SBUF = BN == 128 ? 2 : 1;
-  static constexpr int STAGES = BN == 256 ? 4 : (BN == 192 ? 5 : 6);
+  static constexpr int STAGES = BN == 256 ? 5 : 6;  // as deep as the 227 KB of shared memory allow
   static constexpr uint32_t TMEM_COLS = BN == 128 ? 256 : 512;
   static constexpr int ACC_STRIDE = BN == 128 ? 128 : 256;  // TMEM columns between the two accumulators
   static constexpr int SMEM = STAGES * STAGE_BYTES + NWG * SBUF * OUT_BYTES + 1024 + 256;

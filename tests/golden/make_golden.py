@@ -25,7 +25,8 @@ sys.path.insert(0, str(ROOT))
 from kleinhirn_b200.spec import spec_from_hf_config  # noqa: E402
 from kleinhirn_b200.synthetic import random_weights  # noqa: E402
 
-# Tiny members of the six families: hidden 64, 2 heads (D 32), 1-2 layers, vocabulary 96.
+# Tiny members of the families and head variants: hidden 64, 2 heads (D 32), 1-3 layers,
+# vocabulary 96.
 CASES = [
     {"name": "bert-embed-mean", "seed": 11,
      "config": {"model_type": "bert", "hidden_size": 64, "num_hidden_layers": 2, "num_attention_heads": 2,
@@ -68,6 +69,46 @@ CASES = [
      "extras": {"task": "embeddings", "sentenceTransformers": {"pooling": {"pooling_mode_mean_tokens": True},
                                                                "normalize": True}},
      "lengths": [6, 19, 32]},
+    # ELECTRA: embeddings of width 32 projected to the hidden width (src/plan/build.ts:166-169)
+    {"name": "electra-classify", "seed": 17,
+     "config": {"model_type": "electra", "hidden_size": 64, "embedding_size": 32, "num_hidden_layers": 2,
+                "num_attention_heads": 2, "intermediate_size": 128, "hidden_act": "gelu", "vocab_size": 96,
+                "max_position_embeddings": 80, "type_vocab_size": 2, "layer_norm_eps": 1e-12, "num_labels": 2},
+     "extras": {"task": "sequence-classification"},
+     "lengths": [5, 23]},
+    # DeBERTa-v2 with the convolution after layer 0 (im2col + conv GEMM, src/plan/build.ts:196-210)
+    {"name": "deberta-v2-conv-classify", "seed": 18,
+     "config": {"model_type": "deberta-v2", "hidden_size": 64, "num_hidden_layers": 2, "num_attention_heads": 2,
+                "intermediate_size": 128, "hidden_act": "gelu", "vocab_size": 96, "max_position_embeddings": 64,
+                "type_vocab_size": 0, "layer_norm_eps": 1e-7, "relative_attention": True, "position_buckets": 16,
+                "max_relative_positions": -1, "pos_att_type": ["p2c", "c2p"], "share_att_key": True,
+                "norm_rel_ebd": "layer_norm", "position_biased_input": False, "num_labels": 3,
+                "conv_kernel_size": 3, "conv_act": "tanh",
+                "pooler_hidden_size": 64, "pooler_hidden_act": "gelu"},
+     "extras": {"task": "sequence-classification"},
+     "lengths": [8, 30]},
+    # token classification: one logit row per token (src/plan/build.ts:296-357)
+    {"name": "bert-token", "seed": 19,
+     "config": {"model_type": "bert", "hidden_size": 64, "num_hidden_layers": 2, "num_attention_heads": 2,
+                "intermediate_size": 128, "hidden_act": "gelu", "vocab_size": 96, "max_position_embeddings": 80,
+                "type_vocab_size": 2, "layer_norm_eps": 1e-12, "num_labels": 5},
+     "extras": {"task": "token-classification"},
+     "lengths": [7, 26]},
+    # max and CLS pooling of embedding heads
+    {"name": "bert-embed-max", "seed": 20,
+     "config": {"model_type": "bert", "hidden_size": 64, "num_hidden_layers": 1, "num_attention_heads": 2,
+                "intermediate_size": 128, "hidden_act": "gelu", "vocab_size": 96, "max_position_embeddings": 80,
+                "type_vocab_size": 2, "layer_norm_eps": 1e-12},
+     "extras": {"task": "embeddings", "sentenceTransformers": {"pooling": {"pooling_mode_max_tokens": True},
+                                                               "normalize": True}},
+     "lengths": [4, 21]},
+    {"name": "bert-embed-cls", "seed": 21,
+     "config": {"model_type": "bert", "hidden_size": 64, "num_hidden_layers": 1, "num_attention_heads": 2,
+                "intermediate_size": 128, "hidden_act": "gelu", "vocab_size": 96, "max_position_embeddings": 80,
+                "type_vocab_size": 2, "layer_norm_eps": 1e-12},
+     "extras": {"task": "embeddings", "sentenceTransformers": {"pooling": {"pooling_mode_cls_token": True},
+                                                               "normalize": True}},
+     "lengths": [3, 27]},
 ]
 
 

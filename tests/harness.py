@@ -60,9 +60,9 @@ def cuda_forward_plan(backend, m: Model, id_lists, length: int) -> np.ndarray:
         r.upload(word_rows(m.word_table, inputs, length), mask, types)
         r.run(len(ids))
         o = r.read_output()
-        outs.append(o[: m.cols])
+        outs.append(o[: len(ids) * m.cols] if m.head["type"] == "token" else o[: m.cols])
     r.destroy()
-    return np.stack(outs)
+    return np.stack(outs) if m.head["type"] != "token" else outs
 
 
 def cuda_forward_bulk(backend, m: Model, id_lists, length: int, chunk_tokens: int = 4096) -> np.ndarray:
@@ -73,6 +73,9 @@ def cuda_forward_bulk(backend, m: Model, id_lists, length: int, chunk_tokens: in
     out = bulk.run_batch(lens, emb, types if "typeIds" in plan["inputs"] else None)
     bulk.close()
     r.destroy()
+    if m.head["type"] == "token":  # one row per packed token: split per sequence
+        ends = np.cumsum(lens)
+        return [out[e - n: e].ravel() for e, n in zip(ends, lens)]
     return out
 
 
