@@ -56,7 +56,107 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-out", default="", help="write the per-launch profile of one forward here")
+    ap.add_argument("--workload", default="c5", choices=["c5", "c1", "c2-128", "c2-512", "c3", "c4"],
+                    help="c5: the headline (BASELINE config 5); the others print ms/call (c1-c3, B = 1 plan "
+                         "calls) or seqs/s (c4, 64 ragged sequences) of BASELINE configs 1-4, one GPU")
     return ap.parse_args()
+
+
+# (synthetic configuration, sequence length or None for ragged, f16)
+CONFIG_WORKLOADS = {
+    "c1": ("minilm-l6", 128, False),
+    "c2-128": ("roberta-base", 128, True),
+    "c2-512": ("roberta-base", 512, True),
+    "c3": ("deberta-v3-base", 512, True),
+    "c4": ("modernbert-base", None, True),
+}
+
+
+def run_config(args):
+    """ms per call (B = 1 through the PlanRunner: upload, run, read every call) of configs 1-3, and
+    seqs/s of config 4 (64 ragged sequences through the bulk API), on one GPU, with the device
+    time of the same calls beside it."""
+    import torch
+
+    from kleinhirn_b200 import synthetic
+    from kleinhirn_b200.backend import CudaBackend
+    from kleinhirn_b200.encoder import mask_and_types, packed_inputs, word_rows
+    from kleinhirn_b200.plan import build_plan
+    name, length, f16 = CONFIG_WORKLOADS[args.workload]
+    spec, head = synthetic.model(name)
+    w = synthetic.random_weights(spec, head, seed=args.seed)
+    if f16:
+        w = synthetic.to_f16(w)
+    table = w["embeddings.word.weight"]
+    be = CudaBackend(w)
+    stream = torch.cuda.ExternalStream(be.stream)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clocks:
+        if length is not None:
+            ids = synthetic.token_ids(name, np.array([length]), args.seed)[0]
+            plan = build_plan(spec, head, length, 1, 0, f16)
+            r = be.runner(plan)
+            inputs = [{"inputIds": list(ids)}]
+            mask, types = mask_and_types(spec, inputs, length)
+            rows = word_rows(table, inputs, length)
+            tt = types if "typeIds" in plan["inputs"] else None
+
+            def call():
+                r.upload(rows, mask, tt)
+                r.run(length)
+                return r.read_output()
+            for _ in range(max(3, args.warmup)):
+                call()
+            calls = max(20, args.steps)
+            t0 = time.perf_counter()
+            for _ in range(calls):
+                call()
+            e2e_ms = (time.perf_counter() - t0) * 1000.0 / calls
+            torch.cuda.synchronize()
+            ev0.record(stream)
+            for _ in range(calls):
+                r.run(length)
+            ev1.record(stream)
+            torch.cuda.synchronize()
+            dev_ms = ev0.elapsed_time(ev1) / calls
+            launches = len(r.launches())
+            r.destroy()
+            line = {"metric": f"ms/call B=1 L={length} ({name})", "value": e2e_ms, "unit": "ms",
+                    "higher_is_better": False, "device_ms": dev_ms, "calls": calls}
+        else:
+            lens = synthetic.seq_lengths(name, 64, args.seed)
+            ids = synthetic.token_ids(name, lens, args.seed)
+            emb, types, lens = packed_inputs(spec, table, ids)
+            plan = build_plan(spec, head, 512, 1, 0, f16)
+            r = be.runner(plan)
+            bulk = be.bulk(r, int(lens.sum()), len(lens), args.chunk_tokens)
+            tt = types if "typeIds" in plan["inputs"] else None
+            for _ in range(max(3, args.warmup)):
+                bulk.run_batch(lens, emb, tt)
+            calls = max(20, args.steps)
+            t0 = time.perf_counter()
+            for _ in range(calls):
+                bulk.run_batch(lens, emb, tt)
+            e2e_s = (time.perf_counter() - t0) / calls
+            torch.cuda.synchronize()
+            ev0.record(stream)
+            for _ in range(calls):
+                bulk.run()
+            ev1.record(stream)
+            torch.cuda.synchronize()
+            dev_ms = ev0.elapsed_time(ev1) / calls
+            launches = bulk.last_timing()[1]
+            bulk.close()
+            r.destroy()
+            line = {"metric": f"seqs/sec, 64 ragged sequences ({name})", "value": len(lens) / e2e_s,
+                    "unit": "seqs/s", "higher_is_better": True, "device_seqs_per_s": len(lens) / (dev_ms / 1e3),
+                    "device_ms": dev_ms, "tokens": int(lens.sum()), "calls": calls}
+    line.update({"n_gpus": 1, "dtype": "f16" if f16 else "f32", "data": "synthetic",
+                 "config": {"workload": f"{name} (BASELINE config {args.workload[1]})", "layers": spec["layers"],
+                            "hidden": spec["hidden"]},
+                 "gpu_launches_per_call": launches, "clocks": clocks.summary()})
+    be.dispose()
+    print(json.dumps(line), flush=True)
 
 
 def model_flops(spec: dict, lens: np.ndarray) -> tuple[float, float]:
@@ -231,6 +331,9 @@ def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.workload != "c5":
+        run_config(args)
         return
     world, rank, local = dist_setup(args)
     import torch

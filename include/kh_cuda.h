@@ -60,6 +60,14 @@ int kh_init(const int* devices, int n_devices, kh_ctx** out);
 int kh_add_tensor(kh_ctx* ctx, const char* name, int dtype, const int64_t* shape, int ndim, const void* bytes,
                   size_t len);
 
+/* The word table from the bytes of words.bin (WordsDesc src/words-format.ts:6-18): `rows` rows of
+ * `row_bytes` bytes, each `width` values of dtype (KH_F32 / KH_F16) followed by its checksum word
+ * (wordsView, src/words.ts). Becomes the device tensor `name` [rows, width] without the checksums,
+ * for kh_bulk_set_word_table. The caller has verified the file (fetchWords checks its sha256).
+ * The reference keeps this table on the host; beyond the reference interface. */
+int kh_add_words(kh_ctx* ctx, const char* name, int dtype, int64_t rows, int64_t width, int64_t row_bytes,
+                 const void* bytes, size_t len);
+
 /* Backend.weightBytes (src/backend.ts:32-33): device bytes of the loaded weights. */
 int64_t kh_weight_bytes(const kh_ctx* ctx);
 

@@ -33,6 +33,8 @@ _SIGS = {
     "kh_init": ([ctypes.POINTER(ctypes.c_int), ctypes.c_int, ctypes.POINTER(_P)], ctypes.c_int),
     "kh_add_tensor": ([_P, ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(ctypes.c_int64), ctypes.c_int, _P,
                        ctypes.c_size_t], ctypes.c_int),
+    "kh_add_words": ([_P, ctypes.c_char_p, ctypes.c_int, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _P,
+                      ctypes.c_size_t], ctypes.c_int),
     "kh_weight_bytes": ([_P], ctypes.c_int64),
     "kh_check": ([_P, ctypes.c_char_p, ctypes.c_size_t], ctypes.c_int),
     "kh_plan_create": ([_P, ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(_P)], ctypes.c_int),
@@ -307,6 +309,14 @@ class CudaBackend:
             if name == "embeddings.word.weight":
                 continue
             self.add_tensor(name, arr)
+
+    def add_words(self, name: str, words_bin: bytes | np.ndarray, dtype: str, rows: int, width: int,
+                  row_bytes: int) -> None:
+        """The word table from words.bin bytes (rows of `row_bytes`: values, then a checksum word)."""
+        b = np.frombuffer(words_bin, dtype=np.uint8) if isinstance(words_bin, (bytes, bytearray)) else \
+            np.ascontiguousarray(words_bin).view(np.uint8).reshape(-1)
+        _check(self.lib, self.lib.kh_add_words(self.handle, name.encode(), KH_F16 if dtype == "f16" else KH_F32,
+                                               rows, width, row_bytes, _ptr(b), b.size))
 
     def add_tensor(self, name: str, arr: np.ndarray) -> None:
         a = np.ascontiguousarray(arr)

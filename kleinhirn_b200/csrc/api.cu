@@ -199,6 +199,37 @@ int kh_add_tensor(kh_ctx* ctx, const char* name, int dtype, const int64_t* shape
   });
 }
 
+int kh_add_words(kh_ctx* ctx, const char* name, int dtype, int64_t rows, int64_t width, int64_t row_bytes,
+                 const void* bytes, size_t len) {
+  if (!ctx || !name || (len && !bytes)) {
+    g_err = "kh_add_words: null argument";
+    return KH_ERR_ARG;
+  }
+  Ctx* c = ctx->c.get();
+  return guard(c, Latch::No, [&] {
+    if (dtype != KH_F32 && dtype != KH_F16) throw kh::ArgError("kh_add_words: dtype is neither f32 nor f16");
+    if (c->tensors.count(name)) throw kh::ArgError(std::string("weight ") + name + " loaded twice");
+    const int64_t esz = dtype == KH_F16 ? 2 : 4;
+    if (rows < 1 || width < 1 || row_bytes < width * esz + 4 || row_bytes % 4)
+      throw kh::ArgError("kh_add_words: rows of " + std::to_string(row_bytes) + " bytes cannot hold " +
+                         std::to_string(width) + " values and a checksum word");
+    if (int64_t(len) != rows * row_bytes)  // wordsView, src/words.ts
+      throw kh::ArgError("kh_add_words: " + std::to_string(len) + " bytes, " + std::to_string(rows) + " rows of " +
+                         std::to_string(row_bytes) + " need " + std::to_string(rows * row_bytes));
+    kh::DevTensor t;
+    t.name = name;
+    t.dtype = dtype;
+    t.shape = {rows, width};
+    t.bytes = size_t(rows * width * esz);
+    KH_CUDA(cudaMalloc(&t.ptr, std::max<size_t>(t.bytes, 16)));
+    // the row values without the checksum word after each of them
+    KH_CUDA(cudaMemcpy2D(t.ptr, size_t(width * esz), bytes, size_t(row_bytes), size_t(width * esz), size_t(rows),
+                         cudaMemcpyHostToDevice));
+    c->weight_bytes += int64_t(t.bytes);
+    c->tensors.emplace(t.name, t);
+  });
+}
+
 int64_t kh_weight_bytes(const kh_ctx* ctx) { return ctx ? ctx->c->weight_bytes : 0; }
 
 int kh_check(kh_ctx* ctx, const char* plan_json, size_t len) {
