@@ -84,6 +84,11 @@ struct Params {
   __half* ctx;
   int H, HG, T, window;
   float scale_log2;  // SCALE * log2(e)
+  // DeBERTa relative terms (REL kernels): per packed row [2][H][NP] f32 tables, c2p = q . posKey[p]
+  // and p2c = k . posQuery[p], and the plan's relative index relidx [L][L] (local positions)
+  const float* rel_tables;
+  const uint32_t* relidx;
+  int L, NP;
 };
 
 template <int D>
@@ -92,7 +97,7 @@ __device__ __forceinline__ uint64_t desc_rows(const void* smem) {
   return ((addr >> 4) & 0x3FFFull) | (1ull << 16) | (Cfg<D>::SBO << 32) | (1ull << 46) | (Cfg<D>::LAYOUT << 61);
 }
 
-template <int D>
+template <int D, bool REL = false>
 __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_constant__ CUtensorMap tm, const Params p) {
   using C = Cfg<D>;
   extern __shared__ uint8_t smem_raw[];
@@ -296,10 +301,11 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
     const bool in_range = row < p.T;
     const bool qvalid = in_range && p.mask[row] > 0.5f;
     // packed key rows this query may attend: its own sequence, clamped to the window
-    int lo = 0, hi = 0;
+    int lo = 0, hi = 0, sstart = 0;
     if (qvalid) {
       const int s = p.row_seq[row];
       lo = p.seq_start[s];
+      sstart = lo;
       hi = lo + p.seq_len[s];
       if (p.window > 0) {
         lo = max(lo, row - p.window);
@@ -399,6 +405,24 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
       } else {
 #pragma unroll
         for (int i = 0; i < 64; ++i) sr[i] = 0u;
+      }
+      if constexpr (REL) {
+        // s = q.k + q.posKey[p] + k.posQuery[p], p = relidx[i][j] (local positions), over the kept keys
+        const float* c2p = p.rel_tables + (int64_t(row) * 2 * p.H + hg0 + hh) * p.NP;
+        const uint32_t* ridx = p.relidx + int64_t(row - sstart) * p.L - sstart;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          if (!__any_sync(0xffffffffu, km[c] != 0u)) continue;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            if ((km[c] >> i) & 1u) {
+              const int j = k0 + c * 32 + i;
+              const uint32_t pp = __ldg(ridx + j);
+              const float* p2c = p.rel_tables + ((int64_t(j) * 2 + 1) * p.H + hg0 + hh) * p.NP;
+              sr[c * 32 + i] = __float_as_uint(__uint_as_float(sr[c * 32 + i]) + __ldg(c2p + pp) + __ldg(p2c + pp));
+            }
+          }
+        }
       }
       // the row maximum of the kept raw scores: this half, then both halves
       float mr[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
@@ -539,18 +563,123 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
   }
 }
 
-int heads_per_cta(int H) {
-  for (int g = 4; g > 1; --g)
-    if (H % g == 0) return g;
-  return 1;
+// ---- DeBERTa relative-position tables on the tensor cores ----
+//
+// For every packed row r, head h and relative-position row p of the layer's posKey / posQuery
+// [NP, H D] (f16): table[r][0][h][p] = q_r,h . posKey[p, h] (c2p) and table[r][1][h][p] =
+// k_r,h . posQuery[p, h] (p2c), f32 (src/plan/layers.ts:61-80: the attrel PART 0 / 1 products).
+// One CTA per (128 rows, 256 positions, table, head): one TMA load of each operand, M 128 x N 256
+// x K 64 in four tcgen05 MMAs, the accumulator read back from TMEM and stored as f32 rows.
+struct RelParams {
+  float* out;
+  int T, H, NP;
+};
+
+__global__ void __launch_bounds__(128) relpos_tables_kernel(const __grid_constant__ CUtensorMap tm_qkv,
+                                                            const __grid_constant__ CUtensorMap tm_pk,
+                                                            const __grid_constant__ CUtensorMap tm_pq,
+                                                            const RelParams rp) {
+  constexpr int D = 64;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;           // 128 rows x 64 f16, 128-byte swizzle
+  uint8_t* sB = smem + 16384;   // 256 positions x 64 f16
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 16384 + 32768);
+  uint64_t* full = bars;
+  uint64_t* done = bars + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2);
+  volatile int* bad = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = blockIdx.x * 128, p0 = blockIdx.y * 256;
+  const int t = blockIdx.z / rp.H, h = blockIdx.z - t * rp.H;
+  if (threadIdx.x == 0) {
+    mbar_init(full, 1);
+    mbar_init(done, 1);
+    *bad = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) tmem_alloc(tmem_holder, 256);
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tmem = *tmem_holder;
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(full, 16384 + 32768);
+    tma_load_2d(sA, &tm_qkv, full, (t == 0 ? h : rp.H + h) * D, row0);
+    tma_load_2d(sB, t == 0 ? &tm_pk : &tm_pq, full, h * D, p0);
+    if (mbar_wait(full, 0, 71)) {
+      fence_after_sync();
+      const uint64_t da = desc_sw128(sA), db = desc_sw128(sB);
+#pragma unroll
+      for (int k = 0; k < D / 16; ++k) mma_f16(tmem, da + uint64_t(2 * k), db + uint64_t(2 * k), idesc_f16(128, 256), k ? 1u : 0u);
+    } else {
+      *bad = 1;  // the copies may still land: the commit below waits for nothing issued
+    }
+    mma_commit(done);
+  }
+  __syncwarp();
+  const bool ok = mbar_wait(done, 0, 72) && !*bad;
+  fence_after_sync();
+  const int r = row0 + warp * 32 + lane;
+  const uint32_t taddr = tmem + (uint32_t(warp * 32) << 16);
+  float* dst = rp.out + ((int64_t(r) * 2 + t) * rp.H + h) * rp.NP + p0;
+#pragma unroll 1
+  for (int c = 0; c < 256; c += 32) {
+    uint32_t v[32];
+    tmem_ld32(taddr + c, v);
+    tmem_ld_wait();
+    if (ok && r < rp.T && p0 + c < rp.NP) {
+      if (p0 + c + 32 <= rp.NP && (rp.NP & 3) == 0) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          reinterpret_cast<float4*>(dst + c)[q] = make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                                                             __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (p0 + c + i < rp.NP) dst[c + i] = __uint_as_float(v[i]);
+      }
+    }
+  }
+  if (threadIdx.x == 0 && *bad) mbar_wait(full, 0, 73);  // the loads of a failed wait land before the exit
+  fence_before_sync();
+  __syncthreads();
+  if (warp == 0) {
+    fence_after_sync();
+    tmem_free(tmem, 256);
+  }
 }
 
-template <int D>
+// Heads per CTA: up to 4 (the CTA loads the keys of a tile once for all its heads), fewer when
+// the launch would otherwise leave most SMs idle (short B = 1 calls).
+int heads_per_cta(int H, int tiles) {
+  static const int sms = device_sms();
+  for (int g = 4; g > 1; --g)
+    if (H % g == 0 && int64_t(tiles) * (H / g) >= int64_t(sms)) return g;
+  return 1;
+}
+template <int D, bool REL = false>
 void launch_tc(const AttnArgs& a, const SeqTable& seq, int T, cudaStream_t st) {
   static bool configured = false;
   if (!configured) {
-    KH_CUDA(cudaFuncSetAttribute(attn_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::SMEM));
+    KH_CUDA(cudaFuncSetAttribute(attn_tc_kernel<D, REL>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::SMEM));
+    if (REL)
+      KH_CUDA(cudaFuncSetAttribute(relpos_tables_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 49152 + 1024 + 64));
     configured = true;
+  }
+  if constexpr (REL) {
+    // c2p / p2c tables of every packed row and head first
+    const uint64_t cols = uint64_t(3) * a.H * D, hd = uint64_t(a.H) * D;
+    const CUtensorMap& tq = tensor_map_f16(a.qkv, uint64_t(T), cols, cols, D, 128, 128);
+    const CUtensorMap& tk = tensor_map_f16(a.pos_key, uint64_t(a.np), hd, hd, D, 256, 128);
+    const CUtensorMap& tp = tensor_map_f16(a.pos_query, uint64_t(a.np), hd, hd, D, 256, 128);
+    RelParams rp;
+    rp.out = a.rel_tables;
+    rp.T = T;
+    rp.H = a.H;
+    rp.NP = a.np;
+    const dim3 g((T + 127) / 128, (a.np + 255) / 256, 2 * a.H);
+    relpos_tables_kernel<<<g, 128, 49152 + 1024 + 64, st>>>(tq, tk, tp, rp);
   }
   const uint64_t cols = uint64_t(3) * a.H * D;
   const CUtensorMap& tm = tensor_map_f16(a.qkv, uint64_t(T), cols, cols, D, 128, D * 2);
@@ -562,12 +691,16 @@ void launch_tc(const AttnArgs& a, const SeqTable& seq, int T, cudaStream_t st) {
   p.ptiles = seq.ptiles;
   p.ctx = static_cast<__half*>(a.ctx);
   p.H = a.H;
-  p.HG = heads_per_cta(a.H);
+  p.HG = heads_per_cta(a.H, seq.nptiles);
   p.T = T;
   p.window = a.window;
   p.scale_log2 = a.scale * 1.4426950408889634f;
+  p.rel_tables = a.rel_tables;
+  p.relidx = a.relidx;
+  p.L = a.L;
+  p.NP = a.np;
   dim3 grid(seq.nptiles, a.H / p.HG);
-  attn_tc_kernel<D><<<grid, THREADS, Cfg<D>::SMEM, st>>>(tm, p);
+  attn_tc_kernel<D, REL><<<grid, THREADS, Cfg<D>::SMEM, st>>>(tm, p);
 }
 
 // ---- packed attention whose sequence table lives in static device memory ----
@@ -698,7 +831,7 @@ void attention_f16_noalloc(const void* qkv, const float* mask, void* ctx, const 
   p.ptiles = w + NA_PTILES;
   p.ctx = static_cast<__half*>(ctx);
   p.H = H;
-  p.HG = heads_per_cta(H);
+  p.HG = heads_per_cta(H, int((T + TQ - 1) / TQ));
   p.T = int(T);
   p.window = window;
   p.scale_log2 = scale * 1.4426950408889634f;
@@ -711,9 +844,14 @@ void attention_f16_noalloc(const void* qkv, const float* mask, void* ctx, const 
 int attention_tile_q(bool) { return 64; }
 
 bool attention_tc_supported(bool f16, const AttnArgs& a) {
-  // the key rows of one packed tile must fit the CTA's key-tile masks
-  return f16 && !a.rel && (a.D == 64 || a.D == 32) && a.L <= (MAXKT * TKEYS - TQ) / 2;
+  // the key rows of one packed tile must fit the CTA's key-tile masks; relative attention on the
+  // tensor cores takes 64-wide heads (DeBERTa-v2/v3) and needs its tables (AttnArgs::rel_tables)
+  if (!f16 || a.L > (MAXKT * TKEYS - TQ) / 2) return false;
+  if (a.rel) return a.D == 64 && a.np > 0;
+  return a.D == 64 || a.D == 32;
 }
+
+int64_t attention_rel_table_floats_per_row(int H, int np) { return int64_t(2) * H * np; }
 
 void launch_attention(bool f16, const AttnArgs& a, const SeqTable& seq, cudaStream_t st) {
   if (seq.nptiles <= 0 && seq.ntiles <= 0) return;
@@ -723,8 +861,14 @@ void launch_attention(bool f16, const AttnArgs& a, const SeqTable& seq, cudaStre
   }
   if (seq.nptiles <= 0) return;
   const int T = a.rows;  // packed rows of the launch: the last packed tile ends at T
-  if (a.D == 64) launch_tc<64>(a, seq, T, st);
-  else launch_tc<32>(a, seq, T, st);
+  if (a.rel) {
+    if (!a.rel_tables) throw PlanError("relative attention on the tensor cores without its tables");
+    launch_tc<64, true>(a, seq, T, st);
+  } else if (a.D == 64) {
+    launch_tc<64>(a, seq, T, st);
+  } else {
+    launch_tc<32>(a, seq, T, st);
+  }
 }
 
 int attn_error_code() {

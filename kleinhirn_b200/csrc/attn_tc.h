@@ -11,6 +11,11 @@ int attention_tile_q(bool f16);
 
 void launch_attention(bool f16, const AttnArgs& a, const SeqTable& seq, cudaStream_t st);
 
+// Whether the tensor-core kernel takes this attention (the relative form needs AttnArgs::np and,
+// at launch, AttnArgs::rel_tables of attention_rel_table_floats_per_row floats per packed row).
+bool attention_tc_supported(bool f16, const AttnArgs& a);
+int64_t attention_rel_table_floats_per_row(int H, int np);
+
 // Code of the first tensor-core attention wait that gave up (0: none); read after a sync.
 int attn_error_code();
 

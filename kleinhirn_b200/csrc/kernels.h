@@ -84,6 +84,8 @@ struct AttnArgs {
   const uint32_t* relidx = nullptr;
   int L = 0;           // bucket length: relidx is L x L
   int rows = 0;        // packed rows of the launch
+  int np = 0;          // rows of pos_key / pos_query (relative positions)
+  float* rel_tables = nullptr;  // tensor-core relative attention: [rows][2][H][np] f32 scratch
 };
 void launch_attention_simt(bool f16, const AttnArgs& a, const SeqTable& seq, cudaStream_t st);
 

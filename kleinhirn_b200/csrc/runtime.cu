@@ -223,6 +223,7 @@ void plan_compile(Ctx* ctx, const Json& plan, CompiledPlan& cp) {
     BufInfo b;
     b.id = id;
     b.elem = esz;
+    if (id[0] == '#') return info.emplace(id, b).first->second;  // scratch of this runtime, not in the plan
     auto dit = decl.find(id);
     if (dit == decl.end()) throw PlanError("plan: buffer " + id + " is not declared");
     const Json& d = *dit->second;
@@ -315,14 +316,29 @@ void plan_compile(Ctx* ctx, const Json& plan, CompiledPlan& cp) {
       cb.cols = std::max<int64_t>(cb.cols, int64_t(g.H) * g.D);
       const void* pk = nullptr;
       const void* pq = nullptr;
+      int np = 0;
+      bool rel_tables = false;
       if (g.rel) {
-        pk = ctx->weight(g.pos_key.substr(2), f16).ptr;
+        const DevTensor& tk = ctx->weight(g.pos_key.substr(2), f16);
+        pk = tk.ptr;
         pq = ctx->weight(g.pos_query.substr(2), f16).ptr;
+        np = tk.shape.empty() ? 0 : int(tk.shape[0]);
         use(g.relidx);
+        AttnArgs probe;
+        probe.rel = true; probe.D = g.D; probe.L = g.L; probe.np = np;
+        if (attention_tc_supported(f16, probe)) {
+          // c2p / p2c tables of the tensor-core path: f32 scratch rows shared by every layer
+          rel_tables = true;
+          BufInfo& tb = touch("#reltables");
+          tb.kind = BufInfo::Rows;
+          tb.elem = 4;
+          tb.cols = std::max<int64_t>(tb.cols, attention_rel_table_floats_per_row(g.H, np));
+        }
       }
       protos.push_back({"attention", g.names, [=](const CompiledPlan& c) {
         const int iq = bi(c, g.qkv), im = bi(c, g.mask), ic = bi(c, g.ctx);
         const int ir = g.rel ? bi(c, g.relidx) : -1;
+        const int it = rel_tables ? bi(c, "#reltables") : -1;
         Step s;
         s.run = [=](Exec& ex, cudaStream_t st) {
           AttnArgs a;
@@ -330,6 +346,8 @@ void plan_compile(Ctx* ctx, const Json& plan, CompiledPlan& cp) {
           a.H = g.H; a.D = g.D; a.scale = g.scale; a.window = g.window; a.rel = g.rel;
           a.pos_key = pk; a.pos_query = pq; a.relidx = ir >= 0 ? (const uint32_t*)ex.buf(ir) : nullptr;
           a.L = g.L;
+          a.np = np;
+          a.rel_tables = it >= 0 ? (float*)ex.buf(it) : nullptr;
           a.rows = ex.T;
           launch_attention(f16, a, ex.seq, st);
         };
@@ -588,6 +606,12 @@ void plan_compile(Ctx* ctx, const Json& plan, CompiledPlan& cp) {
     cp.buf_index[id] = int(cp.bufs.size());
     cp.bufs.push_back(b);
   }
+  // scratch of this runtime (not declared by the plan), after the plan's buffers
+  for (const auto& kv : info)
+    if (kv.first[0] == '#') {
+      cp.buf_index[kv.first] = int(cp.bufs.size());
+      cp.bufs.push_back(kv.second);
+    }
   const BufInfo& ob = cp.bufs[cp.buf_index.at(cp.out_buf)];
   cp.out_per_seq = ob.kind == BufInfo::Seqs;
   cp.tile_q = attention_tile_q(cp.f16);

@@ -3,6 +3,8 @@ reference of the reference's own attention test (tests/wasm_plan.test.ts:299-333
 sequences packed into shared 128-row tiles, prefix masks with NaN-poisoned padding rows (they
 must never enter a sum), masked query rows exactly zero, sliding windows, head dimensions 32 and
 64, sequences longer than one 128-key tile."""
+import math
+
 import numpy as np
 import pytest
 
@@ -74,3 +76,85 @@ def test_single_call_rows_below_bucket():
     want = attention_ref(qkv.astype(np.float32), mask, L, 1, H, D, D ** -0.5, 0, 77)
     got = run_attention(qkv, mask, L, 1, H, D, D ** -0.5, 0, 77)
     assert np.allclose(got, want, atol=4e-3, rtol=1e-2), np.abs(got - want).max()
+
+
+def relative_ref(qkv16, mask, L, B, H, D, scale_div, idx, pk16, pq16):
+    """The relative attention of attention_ref (tests/wasm_plan.test.ts:299-376) vectorised, float64."""
+    hd = H * D
+    x = qkv16.astype(np.float64).reshape(B, L, 3, H, D)
+    pk = pk16.astype(np.float64).reshape(-1, H, D)
+    pq = pq16.astype(np.float64).reshape(-1, H, D)
+    p = idx.reshape(L, L).astype(np.int64)
+    m = mask.reshape(B, L) > 0.5
+    out = np.zeros((B, L, H, D))
+    for b in range(B):
+        for h in range(H):
+            q, k, v = x[b, :, 0, h], x[b, :, 1, h], x[b, :, 2, h]
+            qs = np.nan_to_num(q) * m[b][:, None]
+            ks = np.nan_to_num(k) * m[b][:, None]
+            s = qs @ ks.T + (qs @ pk[:, h].T)[np.arange(L)[:, None], p] + (ks @ pq[:, h].T)[np.arange(L)[None, :], p]
+            s = np.where(m[b][None, :], s / scale_div, -np.inf)
+            e = np.exp(s - s.max(axis=1, keepdims=True))
+            pr = e / e.sum(axis=1, keepdims=True)
+            o = pr @ (np.nan_to_num(v) * m[b][:, None])
+            out[b, :, h] = np.where(m[b][:, None], o, 0.0)
+    return out.reshape(-1)[: B * L * hd]
+
+
+def run_relative(qkv16, mask, L, B, H, D, scale_div, idx, pk16, pq16, rows):
+    from kleinhirn_b200.backend import CudaBackend
+    hd = H * D
+    ops = [{"name": "attn", "kernel": "attention", "constants": {"L": L, "H": H, "D": D, "SCALE": scale_div},
+            "bind": ["qkv", "w:pk", "w:pq", "ri", "mask", "ctx"], "dispatch": [H, "rows"]}]
+    plan = {"f16": True, "length": L, "batch": B, "markers": 0, "embeddingSize": 1,
+            "buffers": [{"id": "qkv", "bytes": 2 * B * L * 3 * hd, "usage": "rw"},
+                        {"id": "mask", "bytes": 4 * B * L, "usage": "rw"},
+                        {"id": "ri", "bytes": idx.nbytes, "usage": "rw", "init": idx.tobytes()},
+                        {"id": "ctx", "bytes": 2 * B * L * hd, "usage": "rw"}],
+            "segments": [{"name": "s", "prefix": "", "ops": ops}], "inputs": {"embeddings": "mask", "mask": "mask"},
+            "output": {"buffer": "ctx", "bytes": 2 * B * L * hd, "dtype": "storage", "rows": B * L * hd, "cols": 1},
+            "captureSlots": 0, "captureSlotBytes": 0}
+    be = CudaBackend()
+    be.add_tensor("pk", pk16)
+    be.add_tensor("pq", pq16)
+    r = be.runner(plan)
+    r.write_buffer("qkv", qkv16)
+    r.write_buffer("mask", mask)
+    r.run(rows)
+    labels = r.launches()
+    out = r.read_buffer("ctx", 2 * rows * hd).view(np.float16).astype(np.float64)
+    r.destroy()
+    be.dispose()
+    return out, labels
+
+
+@pytest.mark.parametrize("L,lens,span", [
+    (160, [160, 77, 100], 64),    # three sequences, 128 relative positions
+    (300, [300, 129], 256),       # several key tiles, 512 relative positions (two table tiles)
+])
+def test_relative_attention_f16(L, lens, span):
+    """DeBERTa's disentangled attention on the tensor cores: s_ij = (q_i.k_j + q_i.posKey[p_ij] +
+    k_j.posQuery[p_ij]) / sqrt(3 D) with p_ij = relidx[i][j] (src/plan/layers.ts:61-80,
+    tests/wasm_plan.test.ts:336-376), against float64; NaN-poisoned padding rows."""
+    B, H, D = len(lens), 4, 64
+    hd = H * D
+    rng = np.random.default_rng(L + span)
+    qkv = (rng.standard_normal(B * L * 3 * hd) * 1.2).astype(np.float16)
+    mask = prefix_mask(L, lens)
+    for r in range(B * L):
+        if not mask[r]:
+            qkv[r * 3 * hd:(r + 1) * 3 * hd] = np.nan
+    idx = np.zeros(L * L, dtype=np.uint32)
+    for i in range(L):
+        idx[i * L:(i + 1) * L] = np.clip(i - np.arange(L) + span, 0, 2 * span - 1)
+    pk = (rng.standard_normal((2 * span, hd)) * 0.8).astype(np.float16)
+    pq = (rng.standard_normal((2 * span, hd)) * 0.8).astype(np.float16)
+    scale_div = math.sqrt(3 * D)
+    rows = B * L
+    want = relative_ref(qkv, mask, L, B, H, D, scale_div, idx, pk, pq)
+    got, labels = run_relative(qkv, mask, L, B, H, D, scale_div, idx, pk, pq, rows)
+    keep = np.repeat(mask[:rows] > 0, hd)
+    assert np.all(got[~keep] == 0), "masked query rows must be exactly zero"
+    err = np.abs(got[keep] - want[keep])
+    tol = 4e-3 + 1e-2 * np.abs(want[keep])
+    assert np.all(err <= tol), f"worst {err.max()} at {int(np.argmax(err - tol))}"
