@@ -81,6 +81,24 @@ __device__ __forceinline__ float gelu_as(float v) {
   return fmaf(-(a * hp), e, fmaxf(v, 0.0f));
 }
 
+// gelu_as on two values with packed f32x2 arithmetic (the same operations and roundings: the
+// polynomial's coefficients carry the factor -0.5, so the last step is relu(v) + |v| (-hp) e).
+__device__ __forceinline__ float2 gelu_as2(float2 v) {
+  const float2 a = make_float2(fabsf(v.x), fabsf(v.y));
+  const float2 d = ffma2(a, make_float2(0.3275911f * 0.7071067811865476f, 0.3275911f * 0.7071067811865476f),
+                         make_float2(1.0f, 1.0f));
+  const float2 t = make_float2(rcp_approx(d.x), rcp_approx(d.y));
+  float2 h = ffma2(make_float2(-0.5f * 1.061405429f, -0.5f * 1.061405429f), t,
+                   make_float2(-0.5f * -1.453152027f, -0.5f * -1.453152027f));
+  h = ffma2(h, t, make_float2(-0.5f * 1.421413741f, -0.5f * 1.421413741f));
+  h = ffma2(h, t, make_float2(-0.5f * -0.284496736f, -0.5f * -0.284496736f));
+  h = ffma2(h, t, make_float2(-0.5f * 0.254829592f, -0.5f * 0.254829592f));
+  const float2 nhp = fmul2(h, t);  // -0.5 p(t)
+  const float2 w = fmul2(fmul2(v, v), make_float2(-0.5f * 1.4426950408889634f, -0.5f * 1.4426950408889634f));
+  const float2 e = make_float2(ex2_approx(w.x), ex2_approx(w.y));
+  return ffma2(fmul2(a, nhp), e, make_float2(fmaxf(v.x, 0.0f), fmaxf(v.y, 0.0f)));
+}
+
 __device__ __forceinline__ float act_fn(float v, int act) {
   if (act == 1) return fmaxf(v, 0.0f);
   if (act == 2) return gelu_as(v);
@@ -127,13 +145,20 @@ __device__ __forceinline__ void bias_act32(float (&v)[32], const __half* bias, i
       const __half2* h = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float2 f = __half22float2(h[e]);
-        v[q * 8 + 2 * e] += f.x;
-        v[q * 8 + 2 * e + 1] += f.y;
+        const float2 f = fadd2(make_float2(v[q * 8 + 2 * e], v[q * 8 + 2 * e + 1]), __half22float2(h[e]));
+        v[q * 8 + 2 * e] = f.x;
+        v[q * 8 + 2 * e + 1] = f.y;
       }
     }
   }
-  if constexpr (MODE >= 1 && MODE <= 4) {
+  if constexpr (MODE == 2) {
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) {
+      const float2 g = gelu_as2(make_float2(v[i], v[i + 1]));
+      v[i] = g.x;
+      v[i + 1] = g.y;
+    }
+  } else if constexpr (MODE >= 1 && MODE <= 4) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = act_fn(v[i], MODE);
   }
@@ -332,27 +357,72 @@ __global__ void __launch_bounds__(PCfg<BN>::THREADS, 1)
       if constexpr (MODE == EPI_MODE_GEGLU) {
         constexpr int OC = BN / 2 / NWG;  // outputs of one warpgroup: 32
         static_assert(OC == 32, "geglu warpgroups write 32 outputs");
-        uint32_t ra[32], rb[32];
-        tmem_ld32(taddr + g * 32, ra);
-        tmem_ld32(taddr + BN / 2 + g * 32, rb);
-        tmem_ld_wait();
-        release_acc();
-        named_bar(1 + g, 128);
-        float a[32], b[32];
+        named_bar(1 + g, 128);  // the staging tile is free
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          a[i] = __uint_as_float(ra[i]);
-          b[i] = __uint_as_float(rb[i]);
+        for (int half = 0; half < 2; ++half) {  // 16 outputs at a time
+          uint32_t ra[16], rb[16];
+          tmem_ld16(taddr + g * 32 + 16 * half, ra);
+          tmem_ld16(taddr + BN / 2 + g * 32 + 16 * half, rb);
+          tmem_ld_wait();
+          if (half == 1) release_acc();
+          const uint4* ba = reinterpret_cast<const uint4*>(p.bias + n0 + g * 32 + 16 * half);
+          const uint4* bb = reinterpret_cast<const uint4*>(p.bias + n0 + BN / 2 + g * 32 + 16 * half);
+          uint32_t packed[8];
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            uint4 ua = make_uint4(0, 0, 0, 0), ub = make_uint4(0, 0, 0, 0);
+            if (p.bias) {
+              ua = __ldg(ba + q);
+              ub = __ldg(bb + q);
+            }
+            const __half2* ha = reinterpret_cast<const __half2*>(&ua);
+            const __half2* hb = reinterpret_cast<const __half2*>(&ub);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int i = q * 8 + 2 * e;
+              const float2 av = fadd2(make_float2(__uint_as_float(ra[i]), __uint_as_float(ra[i + 1])), __half22float2(ha[e]));
+              const float2 bv = fadd2(make_float2(__uint_as_float(rb[i]), __uint_as_float(rb[i + 1])), __half22float2(hb[e]));
+              const float2 gl = gelu_as2(make_float2(f16r(av.x), f16r(av.y)));
+              const float2 o = fmul2(gl, make_float2(f16r(bv.x), f16r(bv.y)));
+              __half2 h2 = __floats2half2_rn(o.x, o.y);
+              packed[q * 4 + e] = *reinterpret_cast<uint32_t*>(&h2);
+            }
+          }
+          // row r of the 64-byte-swizzled staging tile: 16-byte chunks 2 half, 2 half + 1
+          uint8_t* row = stile + r * 64;
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const int ch = 2 * half + q;
+            *reinterpret_cast<uint4*>(row + ((ch ^ ((r >> 1) & 3)) * 16)) =
+                make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+          }
         }
-        bias_act32<0>(a, p.bias, n0 + g * 32);
-        bias_act32<0>(b, p.bias, n0 + BN / 2 + g * 32);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) a[i] = gelu_as(f16r(a[i])) * f16r(b[i]);
-        stage32_sw64(stile, r, a);
         fence_proxy_async_smem();
         named_bar(1 + g, 128);
         if (leader) {
           tma_store_2d(&tmC, stile, nb * (BN / 2) + g * 32, row0);
+          bulk_commit();
+        }
+      } else if constexpr (MODE <= 4) {
+        // bias + activation, 32 columns at a time (few registers live for the activation)
+        const int nb0 = min(nc, p.N - 64);
+        named_bar(1 + g, 128);  // the staging tile is free
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t ra[32];
+          tmem_ld32(taddr + g * 64 + 32 * half, ra);
+          tmem_ld_wait();
+          if (half == 1) release_acc();
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(ra[i]);
+          bias_act32<MODE>(v, p.bias, nb0 + 32 * half);
+          stage32_sw128(stile, r, 4 * half, v);
+        }
+        fence_proxy_async_smem();
+        named_bar(1 + g, 128);
+        if (leader) {
+          if (nc < p.N) tma_store_2d(&tmC, stile, nc, row0);
           bulk_commit();
         }
       } else {
@@ -409,10 +479,6 @@ __global__ void __launch_bounds__(PCfg<BN>::THREADS, 1)
               v[o + 2 * e + 1] = f.y + f16r(v[o + 2 * e + 1]);
             }
           }
-        } else {
-          bias_act32<MODE>(v0, p.bias, nb0);
-          bias_act32<MODE>(v1, p.bias, nb0 + 32);
-          named_bar(1 + g, 128);
         }
         stage32_sw128(stile, r, 0, v0);
         stage32_sw128(stile, r, 4, v1);
