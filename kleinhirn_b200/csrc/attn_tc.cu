@@ -323,6 +323,8 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
     // row sum.
     bool started = false;
     float m = 0.f, l = 0.f;
+    bool pending = false;  // the previous head's context is still to be written
+    float l_prev = 0.f;
     auto wwait = [&](uint64_t* bar, uint32_t parity, int code) -> bool {
       const bool r = !*abort_flag && mbar_wait(bar, parity, code);
       return __all_sync(0xffffffffu, r);
@@ -341,17 +343,13 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
     };
     // context row of head hh = O / l over this thread's D / 2 columns (a masked query row, or
     // one without a kept key, is exactly zero: select, not multiply)
-    auto finish_head = [&](int hh) {
-      float lt;
+    // (lt: the row sum of both halves; with tensor-core sums it is read from TMEM here)
+    auto finish_head = [&](int hh, float lt) {
       if constexpr (C::SUMS) {
         uint32_t lr[8];
         tmem_ld8(trow + 192 + uint32_t((hh & 1) * 16), lr);
         tmem_ld_wait();
         lt = __uint_as_float(lr[0]);
-      } else {
-        xsum[((hh & 1) * 2 + hf) * 128 + r_local] = l;
-        named_bar(pair_bar, 64);
-        lt = l + xsum[((hh & 1) * 2 + (hf ^ 1)) * 128 + r_local];
       }
       const bool live = qvalid && lt > 0.f;
       const float inv = live ? 1.0f / lt : 0.f;
@@ -375,10 +373,11 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
       // A failed wait never ends one warp of a pair alone: the pair decides together at its
       // named barriers (bar.red), so neither warp is left waiting at one.
       bool fail = !ok;
-      if (j == 0 && it > 0) {  // a new head: write the previous one and start over
-        if (!fail) fail = !wait_pv(it - 1);
-        if (named_bar_any(pair_bar, 64, fail)) { ok = false; break; }
-        finish_head(hh - 1);
+      if (j == 0 && it > 0) {
+        // a new head starts over; the previous one is written further down, once its last PV
+        // product is done (its O stays in the other TMEM buffer meanwhile)
+        pending = true;
+        l_prev = l;
         started = false;
         l = 0.f;
       }
@@ -443,9 +442,13 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
       }
       const float pm = fmaxf(fmaxf(mr[0], mr[1]), fmaxf(mr[2], mr[3]));
       float* xm = xmax + ((it & 1) * 2) * 128;
+      float* xl = xsum + ((it & 1) * 2) * 128;
       xm[hf * 128 + r_local] = pm;
+      if constexpr (!C::SUMS) xl[hf * 128 + r_local] = l_prev;  // the finished head's half sum
       if (named_bar_any(pair_bar, 64, fail)) { ok = false; break; }
       const float mraw = fmaxf(pm, xm[(hf ^ 1) * 128 + r_local]);
+      float lt_prev = 0.f;
+      if constexpr (!C::SUMS) lt_prev = l_prev + xl[(hf ^ 1) * 128 + r_local];
       float corr = 1.f;
       if (mraw > -INFINITY) {
         const float cand = mraw * p.scale_log2;
@@ -488,7 +491,6 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
           }
         }
         tmem_st_wait();
-        l *= corr;
       }
       // p = exp2(s scale log2e - m) in f16, into this row of P block hf (128-byte swizzled)
       float ls[4] = {0.f, 0.f, 0.f, 0.f};
@@ -505,8 +507,10 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
 #pragma unroll
             for (int e2 = 0; e2 < 4; ++e2) {
               const int i = 8 * q + 2 * e2;
-              const float x0 = ex2_approx(fmaf(__uint_as_float(sr[32 * c + i]), p.scale_log2, -m));
-              const float x1 = ex2_approx(fmaf(__uint_as_float(sr[32 * c + i + 1]), p.scale_log2, -m));
+              const float2 xx = ffma2(make_float2(__uint_as_float(sr[32 * c + i]), __uint_as_float(sr[32 * c + i + 1])),
+                                      make_float2(p.scale_log2, p.scale_log2), make_float2(-m, -m));
+              const float x0 = ex2_approx(xx.x);
+              const float x1 = ex2_approx(xx.y);
               if constexpr (!C::SUMS) {
                 ls[i & 3] += x0;
                 ls[(i + 1) & 3] += x1;
@@ -518,10 +522,14 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
 #pragma unroll
             for (int e2 = 0; e2 < 4; ++e2) {
               float pv[2];
+              const int i0 = 8 * q + 2 * e2;
+              const float2 xx = ffma2(make_float2(__uint_as_float(sr[32 * c + i0]), __uint_as_float(sr[32 * c + i0 + 1])),
+                                      make_float2(p.scale_log2, p.scale_log2), make_float2(-m, -m));
+              const float xs[2] = {xx.x, xx.y};
 #pragma unroll
               for (int e = 0; e < 2; ++e) {
-                const int i = 8 * q + 2 * e2 + e;
-                const float x = ex2_approx(fmaf(__uint_as_float(sr[32 * c + i]), p.scale_log2, -m));
+                const int i = i0 + e;
+                const float x = ex2_approx(xs[e]);
                 pv[e] = ((k >> i) & 1u) ? x : 0.f;
                 if constexpr (!C::SUMS) ls[i & 3] += pv[e];
               }
@@ -533,7 +541,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
           *reinterpret_cast<uint4*>(prow + ((ch ^ (r_local & 7)) * 16)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
       }
-      l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+      l = l * corr + ((ls[0] + ls[1]) + (ls[2] + ls[3]));  // (corr rescales the sum so far)
       // value rows of masked or absent keys become zero before the PV product
       const int vs = it % C::VS;
       if (!wwait(&v_full[vs], uint32_t(it / C::VS) & 1, 42)) {
@@ -549,10 +557,18 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
       fence_proxy_async_smem();
       fence_before_sync();
       mbar_arrive(p_full);
+      if (pending) {  // the previous head's PV products are all done; its O is in the other buffer
+        finish_head(hh - 1, lt_prev);
+        pending = false;
+      }
     }
     if (ok && NI > 0) ok = wait_pv(NI - 1);
+    // the last head's half sums cross in the exchange slots of item NI (free: the partner read
+    // those of item NI - 2 before it passed the barrier of item NI - 1)
+    float* xl_end = xsum + ((NI & 1) * 2) * 128;
+    if constexpr (!C::SUMS) xl_end[hf * 128 + r_local] = l;
     if (named_bar_any(pair_bar, 64, !ok)) ok = false;
-    else if (NI > 0) finish_head(HG - 1);
+    else if (NI > 0) finish_head(HG - 1, C::SUMS ? 0.f : l + xl_end[(hf ^ 1) * 128 + r_local]);
     if (!ok) *abort_flag = 1;
   }
   fence_before_sync();
