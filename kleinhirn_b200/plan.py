@@ -255,7 +255,8 @@ def _elements_written(op: dict) -> int:
 
 def build_plan(spec: dict, head: dict, length: int, batch: int = 1, markers: int = 0, f16: bool = True,
                tensor_names=None) -> dict:
-    """src/plan/build.ts:109-526 for the encoder heads (classify, token, embed)."""
+    """src/plan/build.ts:109-526: the encoder heads (classify, token, embed) and the marker
+    heads (gliner2, julia: ``markers`` per sequence, or the Julia option count)."""
     names = tensor_names or tensor_names_for(spec["family"], spec)
     H = spec["hidden"]
     E = spec["embeddingSize"]
@@ -265,10 +266,11 @@ def build_plan(spec: dict, head: dict, length: int, batch: int = 1, markers: int
 
     M = length * batch
     pooled_head = head["type"] in ("classify", "token", "embed")
-    if not pooled_head:
-        raise ValueError(f"head {head['type']} is outside the encoder heads this backend plans")
-    markers = 0
+    if not pooled_head and head["type"] not in ("gliner2", "julia"):
+        raise ValueError(f"head {head['type']} has no plan")
+    markers = head["options"] if head["type"] == "julia" else 0 if pooled_head else markers
     K = markers * batch
+    K16 = math.ceil(K / 16)
     eps = spec["block"]["norm"]["eps"]
     dims = {"hidden": H, "heads": spec["heads"], "headDim": spec["headDim"],
             "intermediate": spec["intermediate"], "rows": M, "length": length, "eps": eps}
@@ -393,51 +395,92 @@ def build_plan(spec: dict, head: dict, length: int, batch: int = 1, markers: int
 
     head_buffers: list[dict] = []
     need_first = False
-    per_row = head["type"] == "token"
-    rows = M if per_row else batch
-    rows16 = "rows16" if per_row else math.ceil(batch / 16)
-    prev = stream
-    width = H
-    ops = []
-    if not per_row:
-        pool = "first" if head.get("pool") == "cls" else head.get("pool")
-        if pool == "first":
-            need_first = True
-            ops.append({"name": "gather", "kernel": "gather", "constants": {"K": 1, "D": H, "L": length},
-                        "bind": ["first", stream, "states"], "dispatch": [1, 1]})
-        else:
-            ops.append({"name": "pool", "kernel": "pool",
-                        "constants": {"L": length, "N": H, "MODE": 0 if pool == "mean" else 1},
-                        "bind": [stream, "mask", "states"], "dispatch": [math.ceil(H / 64), batch]})
-        head_buffers.append({"id": "states", "elements": batch * H, "final": False})
-        prev = "states"
-    steps = head["steps"]
-    for i, step in enumerate(steps):
-        last = i == len(steps) - 1
-        dst = "out" if last else f"hd{i}"
-        if step["op"] == "norm":
-            ops.append({"name": f"step{i}", "kernel": "layernorm",
-                        "constants": {"N": width, "MODE": 0, "EPS": step["eps"]},
-                        "bind": [prev, "dummy", f"w:{step['name']}.weight",
-                                 f"w:{step['name']}.bias" if step["bias"] else "zero", "mask", dst],
-                        "dispatch": ["rows" if per_row else batch, 1]})
-            head_buffers.append({"id": dst, "elements": rows * width, "final": last})
+    row_select = None
+    out_buffer, out_rows, out_cols = "logits", K, 1
+    if pooled_head:
+        per_row = head["type"] == "token"
+        rows = M if per_row else batch
+        rows16 = "rows16" if per_row else math.ceil(batch / 16)
+        prev = stream
+        width = H
+        ops = []
+        if not per_row:
+            pool = "first" if head.get("pool") == "cls" else head.get("pool")
+            if pool == "first":
+                need_first = True
+                ops.append({"name": "gather", "kernel": "gather", "constants": {"K": 1, "D": H, "L": length},
+                            "bind": ["first", stream, "states"], "dispatch": [1, 1]})
+            else:
+                ops.append({"name": "pool", "kernel": "pool",
+                            "constants": {"L": length, "N": H, "MODE": 0 if pool == "mean" else 1},
+                            "bind": [stream, "mask", "states"], "dispatch": [math.ceil(H / 64), batch]})
+            head_buffers.append({"id": "states", "elements": batch * H, "final": False})
+            prev = "states"
+        steps = head["steps"]
+        for i, step in enumerate(steps):
+            last = i == len(steps) - 1
+            dst = "out" if last else f"hd{i}"
+            if step["op"] == "norm":
+                ops.append({"name": f"step{i}", "kernel": "layernorm",
+                            "constants": {"N": width, "MODE": 0, "EPS": step["eps"]},
+                            "bind": [prev, "dummy", f"w:{step['name']}.weight",
+                                     f"w:{step['name']}.bias" if step["bias"] else "zero", "mask", dst],
+                            "dispatch": ["rows" if per_row else batch, 1]})
+                head_buffers.append({"id": dst, "elements": rows * width, "final": last})
+                prev = dst
+                continue
+            if step["in"] != width:
+                raise ValueError(f"head step {step['name']}: input {step['in']}, previous width {width}")
+            ops.append(mm(f"step{i}", rows, step["out"], step["in"], 0 if step["act"] == "none" else act_code(step["act"]),
+                          [prev, f"w:{step['name']}.weight", f"w:{step['name']}.bias" if step["bias"] else "zero", dst],
+                          rows16))
+            head_buffers.append({"id": dst, "elements": rows * step["out"], "final": last})
             prev = dst
-            continue
-        if step["in"] != width:
-            raise ValueError(f"head step {step['name']}: input {step['in']}, previous width {width}")
-        ops.append(mm(f"step{i}", rows, step["out"], step["in"], 0 if step["act"] == "none" else act_code(step["act"]),
-                      [prev, f"w:{step['name']}.weight", f"w:{step['name']}.bias" if step["bias"] else "zero", dst],
-                      rows16))
-        head_buffers.append({"id": dst, "elements": rows * step["out"], "final": last})
-        prev = dst
-        width = step["out"]
-    if not steps:
-        if per_row:
-            raise ValueError("a token head needs at least one dense step")
-        next(b for b in head_buffers if b["id"] == "states")["final"] = True
-    out_buffer, out_rows, out_cols = prev, rows, width
-    segments.append({"name": "head", "prefix": "head.", "ops": ops})
+            width = step["out"]
+        if not steps:
+            if per_row:
+                raise ValueError("a token head needs at least one dense step")
+            next(b for b in head_buffers if b["id"] == "states")["final"] = True
+        out_buffer, out_rows, out_cols = prev, rows, width
+        segments.append({"name": "head", "prefix": "head.", "ops": ops})
+    elif head["type"] == "gliner2":
+        hh = head["hidden"]
+        segments.append({"name": "head", "prefix": "head.", "ops": [
+            {"name": "gather", "kernel": "gather", "constants": {"K": markers, "D": H, "L": length},
+             "bind": ["packed", stream, "states"], "dispatch": [1, 1]},
+            mm("fc1", K, hh, H, 1, ["states", "w:head.fc1.weight", "w:head.fc1.bias", "h1"], K16),
+            mm("fc2", K, 1, hh, 0, ["h1", "w:head.fc2.weight", "w:head.fc2.bias", "raw"], K16),
+            {"name": "maskl", "kernel": "masklogits", "constants": {"K": markers, "TEMP": head["temperature"]},
+             "bind": ["raw", "packed", "logits"], "dispatch": [1, 1]},
+        ]})
+    else:
+        if stream != "tmp":
+            raise ValueError("julia head expects a final norm")
+        segments.append({"name": "typed", "prefix": "", "ops": [
+            {"name": "type", "kernel": "add", "constants": {"TOTAL": M * H, "N": H, "MODE": 1, "L": length},
+             "bind": ["tmp", "typeRow"], "dispatch": [add_workgroups(M, H), 1]}], "capture": take("tmp")})
+        row_select = {"table": "w:type_emb.weight", "dst": "typeRow", "rowBytes": bytes_of(H)}
+        for i in range(head["layers"]):
+            p = f"head.{i}"
+            t = {"qkvW": f"{p}.in_proj.weight", "qkvB": f"{p}.in_proj.bias",
+                 "attnOutW": f"{p}.out_proj.weight", "attnOutB": f"{p}.out_proj.bias",
+                 "attnNormW": f"{p}.norm1.weight", "attnNormB": f"{p}.norm1.bias",
+                 "ffnNormW": f"{p}.norm2.weight", "ffnNormB": f"{p}.norm2.bias",
+                 "ffnInW": f"{p}.linear1.weight", "ffnInB": f"{p}.linear1.bias",
+                 "ffnOutW": f"{p}.linear2.weight", "ffnOutB": f"{p}.linear2.bias"}
+            segments.append({"name": f"head{i}", "prefix": f"head{i}.",
+                             "ops": pre_norm_layer(dims, t, "tmp", True, (H / spec["heads"]) ** -0.5, 0, False,
+                                                   {"kind": "mlp", "width": head["ffn"], "act": 1}),
+                             "capture": take("tmp")})
+        segments.append({"name": "scorer", "prefix": "scorer.", "ops": [
+            {"name": "gather", "kernel": "gather", "constants": {"K": markers, "D": H, "L": length},
+             "bind": ["packed", "tmp", "states"], "dispatch": [1, 1]},
+            ln("ln", 0, ["states", "dummy", "w:scorer.norm.weight", "w:scorer.norm.bias", "mask", "kNormed"], H, K),
+            mm("fc1", K, H, H, 2, ["kNormed", "w:scorer.fc1.weight", "w:scorer.fc1.bias", "h1"], K16),
+            mm("fc2", K, 1, H, 0, ["h1", "w:scorer.fc2.weight", "w:scorer.fc2.bias", "raw"], K16),
+            {"name": "maskl", "kernel": "masklogits", "constants": {"K": markers, "TEMP": 1.0},
+             "bind": ["raw", "packed", "logits"], "dispatch": [1, 1]},
+        ]})
 
     all_ops = [op for s in segments for op in s.get("captureOps", []) + s["ops"]]
     cols: dict[str, int] = {}
@@ -487,10 +530,14 @@ def build_plan(spec: dict, head: dict, length: int, batch: int = 1, markers: int
         st("scores", max(o["constants"]["ROWS"] * o["constants"]["H"] * o["constants"]["L"] * 4 for o in score_ops))
     if any("dummy" in o["bind"] for o in all_ops):
         st("dummy", 4, "storage")
-    for b in head_buffers:
-        st(b["id"], bytes_of(b["elements"]), "logits" if b["final"] else "rw")
-    if need_first:
-        st("first", 3 * batch * 4, "rw", np.zeros(3 * batch, dtype=np.uint32).tobytes())
+    if pooled_head:
+        for b in head_buffers:
+            st(b["id"], bytes_of(b["elements"]), "logits" if b["final"] else "rw")
+        if need_first:
+            st("first", 3 * batch * 4, "rw", np.zeros(3 * batch, dtype=np.uint32).tobytes())
+    else:
+        st("packed", 3 * K * 4)
+        st("logits", K * 4, "logits")
     if rel:
         table = rel_pos_table(length, rel["buckets"], rel["maxPositions"])
         st("relidx", table.nbytes, "rw", table.tobytes())
@@ -502,6 +549,8 @@ def build_plan(spec: dict, head: dict, length: int, batch: int = 1, markers: int
         lo = rope_table(length, rope["thetaLocal"], spec["headDim"])
         st("cossinG", g.nbytes, "rw", g.tobytes())
         st("cossinL", lo.nbytes, "rw", lo.tobytes())
+    if row_select:
+        st("typeRow", bytes_of(batch * H))
     zero_uses = [o for o in all_ops if "zero" in o["bind"]]
     if zero_uses:
         width_z = max(o["constants"]["N"] for o in zero_uses)
@@ -509,15 +558,21 @@ def build_plan(spec: dict, head: dict, length: int, batch: int = 1, markers: int
 
     validate_segments(segments, {d["id"] for d in decls})
     inputs = {"embeddings": "emb", "mask": "mask"}
-    if absolute or embed["typeVocab"] > 0:
+    if not pooled_head:
+        inputs["markers"] = "packed"
+    elif absolute or embed["typeVocab"] > 0:
         inputs["typeIds"] = "typeIds"
-    return {
+    plan = {
         "f16": f16, "length": length, "batch": batch, "markers": markers, "embeddingSize": E,
         "buffers": decls, "segments": segments, "inputs": inputs,
-        "output": {"buffer": out_buffer, "bytes": bytes_of(out_rows * out_cols), "dtype": "storage",
-                   "rows": out_rows, "cols": out_cols},
+        "output": ({"buffer": out_buffer, "bytes": bytes_of(out_rows * out_cols), "dtype": "storage",
+                    "rows": out_rows, "cols": out_cols} if pooled_head else
+                   {"buffer": "logits", "bytes": K * 4, "dtype": "f32", "rows": K, "cols": 1}),
         "captureSlots": slot[0], "captureSlotBytes": length * H * 4,
     }
+    if row_select:
+        plan["rowSelect"] = row_select
+    return plan
 
 
 def plan_to_json(plan: dict) -> str:

@@ -527,6 +527,8 @@ def manifest_tensor_shapes(spec: dict, head: dict) -> dict[str, tuple[int, ...]]
         out[names.finalNormW] = (H,)
         if names.finalNormB:
             out[names.finalNormB] = (H,)
+    if head["type"] in ("gliner2", "julia"):
+        out.update(marker_head_tensor_shapes(spec, head))
     if head["type"] in ("classify", "token", "embed"):
         for s in head["steps"]:
             if s["op"] == "norm":
@@ -537,4 +539,74 @@ def manifest_tensor_shapes(spec: dict, head: dict) -> dict[str, tuple[int, ...]]
                 out[f"{s['name']}.weight"] = (s["out"], s["in"])
                 if s["bias"]:
                     out[f"{s['name']}.bias"] = (s["out"],)
+    return out
+
+
+def spec_from_gliner_manifest(enc: dict, head: dict, markers: int = 16) -> tuple[dict, dict]:
+    """src/plan/spec.ts:212-246: the GLiNER2 span classifier, a DeBERTa-v3 encoder (relative
+    attention, no absolute positions, no type table) and the marker head. ``enc`` holds the
+    manifest ``encoder`` fields (hiddenSize, layers, heads, intermediateSize, positionBuckets,
+    maxRelativePositions, layerNormEps, vocabSize); ``head`` temperature and hiddenSize."""
+    head_dim = enc["hiddenSize"] // enc["heads"]
+    norm = {"eps": enc["layerNormEps"], "bias": True}
+    spec = {
+        "family": "deberta-v2", "hidden": enc["hiddenSize"], "layers": enc["layers"], "heads": enc["heads"],
+        "headDim": head_dim, "intermediate": enc["intermediateSize"], "vocab": enc.get("vocabSize") or 0,
+        "embeddingSize": enc["hiddenSize"],
+        "embed": {"positions": "none", "positionOffset": 0, "maxPositions": 0, "typeVocab": 0, "norm": norm,
+                  "maskMultiply": True, "project": False},
+        "attention": {"kind": "deberta-relative", "bias": True, "scale": 1 / math.sqrt(3 * head_dim),
+                      "rel": {"buckets": enc["positionBuckets"], "maxPositions": enc["maxRelativePositions"],
+                              "types": ["c2p", "p2c"]}},
+        "block": {"order": "post", "firstNormIdentity": False, "finalNorm": False, "norm": norm},
+        "ffn": {"kind": "mlp", "act": "gelu", "bias": True},
+    }
+    return spec, {"type": "gliner2", "hidden": int(head.get("hiddenSize") or 768),
+                  "temperature": head["temperature"], "markers": markers}
+
+
+def spec_from_julia_manifest(enc: dict) -> tuple[dict, dict]:
+    """src/plan/spec.ts:248-276: Julia, a ModernBERT encoder without biases (RoPE, local
+    windows) and the typed head (type row, pre-norm head layers, marker scorer). ``enc`` holds
+    layers, hiddenSize, heads, intermediate, normEps, ropeTheta, localAttention, globalEvery,
+    headLayers, headFfn, options, maxPos, vocab."""
+    head_dim = enc["hiddenSize"] // enc["heads"]
+    norm = {"eps": enc["normEps"], "bias": False}
+    spec = {
+        "family": "modernbert", "hidden": enc["hiddenSize"], "layers": enc["layers"], "heads": enc["heads"],
+        "headDim": head_dim, "intermediate": enc["intermediate"], "vocab": enc.get("vocab") or 0,
+        "embeddingSize": enc["hiddenSize"],
+        "embed": {"positions": "none", "positionOffset": 0, "maxPositions": enc.get("maxPos") or 0, "typeVocab": 0,
+                  "norm": norm, "maskMultiply": False, "project": False},
+        "attention": {"kind": "standard", "bias": False, "scale": head_dim ** -0.5,
+                      "rope": {"thetaGlobal": enc["ropeTheta"], "thetaLocal": enc["ropeTheta"]},
+                      "window": {"half": enc["localAttention"], "globalEvery": enc["globalEvery"]}},
+        "block": {"order": "pre", "firstNormIdentity": True, "finalNorm": True, "norm": norm},
+        "ffn": {"kind": "geglu", "act": "gelu", "bias": False},
+    }
+    return spec, {"type": "julia", "layers": enc["headLayers"], "ffn": enc["headFfn"], "options": enc["options"]}
+
+
+def marker_head_tensor_shapes(spec: dict, head: dict, qtypes: int = 3) -> dict[str, tuple[int, ...]]:
+    """Tensors of the marker heads (src/plan/build.ts:358-430): GLiNER2 fc1/fc2; Julia's type
+    table (``qtypes`` rows), head layers (nn.TransformerEncoderLayer names) and scorer."""
+    H = spec["hidden"]
+    if head["type"] == "gliner2":
+        hh = head["hidden"]
+        return {"head.fc1.weight": (hh, H), "head.fc1.bias": (hh,), "head.fc2.weight": (1, hh),
+                "head.fc2.bias": (1,)}
+    if head["type"] != "julia":
+        raise ValueError(f"head {head['type']} is not a marker head")
+    out: dict[str, tuple[int, ...]] = {"type_emb.weight": (qtypes, H)}
+    F = head["ffn"]
+    for i in range(head["layers"]):
+        p = f"head.{i}"
+        out.update({f"{p}.in_proj.weight": (3 * H, H), f"{p}.in_proj.bias": (3 * H,),
+                    f"{p}.out_proj.weight": (H, H), f"{p}.out_proj.bias": (H,),
+                    f"{p}.norm1.weight": (H,), f"{p}.norm1.bias": (H,),
+                    f"{p}.norm2.weight": (H,), f"{p}.norm2.bias": (H,),
+                    f"{p}.linear1.weight": (F, H), f"{p}.linear1.bias": (F,),
+                    f"{p}.linear2.weight": (H, F), f"{p}.linear2.bias": (H,)})
+    out.update({"scorer.norm.weight": (H,), "scorer.norm.bias": (H,), "scorer.fc1.weight": (H, H),
+                "scorer.fc1.bias": (H,), "scorer.fc2.weight": (1, H), "scorer.fc2.bias": (1,)})
     return out
