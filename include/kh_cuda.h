@@ -90,6 +90,16 @@ int kh_plan_info(const kh_plan* plan, int* length, int* batch, int* out_rows, in
 int kh_upload(kh_plan* plan, const void* emb, size_t emb_bytes, const float* mask, size_t mask_len,
               const uint32_t* type_ids, size_t type_len);
 
+/* The marker part of RunInput for GLiNER2 / Julia plans (src/plan/executor.ts:25-37 packedMarkers
+ * and qtype; uploads :366-388; type rows :236-246). `packed`: 3 * markers u32 per sequence of the
+ * plan's batch — marker row indices local to the sequence, the marker mask as f32 bits, the
+ * groups. `qtypes`: the Julia type of each sequence, a row of the plan's rowSelect table (null or
+ * fewer entries: type 0, as `qtype ?? 0`; ignored by plans without type rows). Needed once
+ * before kh_run for plans with a markers
+ * input ("plan needs packedMarkers"); a qtype outside the table is KH_ERR_ARG. */
+int kh_upload_markers(kh_plan* plan, const uint32_t* packed, size_t packed_len, const int32_t* qtypes,
+                      size_t n_qtypes);
+
 /* PlanRunner.run (src/backend.ts:21-23): one forward over `rows` rows — the real rows of a
  * B = 1 call (1 <= rows <= length), or length * batch for a batch plan. */
 int kh_run(kh_plan* plan, int rows);
@@ -97,6 +107,17 @@ int kh_run(kh_plan* plan, int rows);
 /* PlanRunner.readOutput (src/backend.ts:24, src/plan/executor.ts:398-408): blocks until the
  * run is done and writes out_rows * out_cols f32 values (f16 storage converted). */
 int kh_read_output(kh_plan* plan, float* out, size_t n);
+
+/* Layer capture, the parity tool of PlanRunner.run(seqLen, capture = true) / readCapture /
+ * assertCapturable (src/backend.ts:21-26; src/plan/executor.ts:178-186, :232, :267-281,
+ * :418-424). kh_capture_check: KH_OK when the plan can capture (f32, batch 1), else KH_ERR_ARG
+ * with the reference's reason. kh_run_capture: one forward over the full bucket that also runs
+ * each segment's captureOps and, after the segment, copies the first captureSlotBytes of each of
+ * its capture buffers into that buffer's slot. kh_read_capture: blocks, then writes the
+ * captureSlots * captureSlotBytes / 4 f32 values. */
+int kh_capture_check(const kh_plan* plan);
+int kh_run_capture(kh_plan* plan);
+int kh_read_capture(kh_plan* plan, float* out, size_t n);
 
 /* PlanRunner.destroy (src/backend.ts:27). */
 void kh_plan_destroy(kh_plan* plan);

@@ -41,6 +41,10 @@ _SIGS = {
     "kh_plan_info": ([_P, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int),
                       ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int64)], ctypes.c_int),
     "kh_upload": ([_P, _P, ctypes.c_size_t, _P, ctypes.c_size_t, _P, ctypes.c_size_t], ctypes.c_int),
+    "kh_upload_markers": ([_P, _P, ctypes.c_size_t, _P, ctypes.c_size_t], ctypes.c_int),
+    "kh_capture_check": ([_P], ctypes.c_int),
+    "kh_run_capture": ([_P], ctypes.c_int),
+    "kh_read_capture": ([_P, _P, ctypes.c_size_t], ctypes.c_int),
     "kh_run": ([_P, ctypes.c_int], ctypes.c_int),
     "kh_read_output": ([_P, _P, ctypes.c_size_t], ctypes.c_int),
     "kh_plan_destroy": ([_P], None),
@@ -144,9 +148,11 @@ class CudaPlanRunner:
     def bytes(self) -> int:
         return self._bytes
 
-    def upload(self, embeddings: np.ndarray, mask: np.ndarray, type_ids: np.ndarray | None = None) -> None:
-        """RunInput (src/plan/executor.ts:25-32): embeddings f16 (or f16 bits as uint16) for f16 plans,
-        f32 otherwise; mask f32; typeIds u32."""
+    def upload(self, embeddings: np.ndarray, mask: np.ndarray, type_ids: np.ndarray | None = None,
+               packed_markers: np.ndarray | None = None, qtype=None) -> None:
+        """RunInput (src/plan/executor.ts:25-37): embeddings f16 (or f16 bits as uint16) for f16 plans,
+        f32 otherwise; mask f32; typeIds u32; for GLiNER2 / Julia plans packedMarkers u32 (3 K per
+        sequence) and qtype (an int, or one per sequence)."""
         want = np.float16 if self.f16 else np.float32
         emb = np.ascontiguousarray(embeddings)
         if emb.dtype == np.uint16 and self.f16:
@@ -157,10 +163,23 @@ class CudaPlanRunner:
         t = None if type_ids is None else np.ascontiguousarray(type_ids, dtype=np.uint32)
         _check(self.lib, self.lib.kh_upload(self.handle, _ptr(emb), emb.nbytes, _ptr(m), m.size, _ptr(t),
                                             0 if t is None else t.size))
+        if packed_markers is not None or "markers" in self.plan["inputs"]:
+            if packed_markers is None:
+                raise KhError(1, "plan needs packedMarkers")
+            pk = np.ascontiguousarray(packed_markers, dtype=np.uint32)
+            q = None
+            if qtype is not None:
+                q = np.ascontiguousarray(np.atleast_1d(np.asarray(qtype)), dtype=np.int32)
+            _check(self.lib, self.lib.kh_upload_markers(self.handle, _ptr(pk), pk.size, _ptr(q),
+                                                        0 if q is None else q.size))
 
     def run(self, seq_len: int, capture: bool = False) -> None:
+        """One forward over seq_len rows; with capture, over the full bucket, filling the capture
+        slots (src/plan/executor.ts:232, :267-281)."""
         if capture:
             self.assert_capturable()
+            _check(self.lib, self.lib.kh_run_capture(self.handle))
+            return
         _check(self.lib, self.lib.kh_run(self.handle, int(seq_len)))
 
     def read_output(self) -> np.ndarray:
@@ -168,12 +187,18 @@ class CudaPlanRunner:
         _check(self.lib, self.lib.kh_read_output(self.handle, _ptr(out), out.size))
         return out
 
-    def read_capture(self):
-        raise NotImplementedError("capture is a WebGPU parity tool (src/plan/executor.ts:84-91)")
+    def read_capture(self) -> np.ndarray:
+        """captureSlots x captureSlotBytes / 4 f32 values of the last capture run
+        (src/plan/executor.ts:418-424)."""
+        self.assert_capturable()
+        out = np.empty(self.plan.get("captureSlots", 0) * self.plan.get("captureSlotBytes", 0) // 4,
+                       dtype=np.float32)
+        _check(self.lib, self.lib.kh_read_capture(self.handle, _ptr(out), out.size))
+        return out
 
     def assert_capturable(self) -> None:
-        # The WASM backend throws the same way (src/wasm-backend.ts:90-96).
-        raise NotImplementedError("the CUDA backend has no capture mode")
+        """Throws unless the plan can capture: f32 and batch 1 (src/plan/executor.ts:178-186)."""
+        _check(self.lib, self.lib.kh_capture_check(self.handle))
 
     def write_buffer(self, bid: str, data: np.ndarray) -> None:
         """Raw bytes into a plan buffer (WasmPlan.view for tests, src/plan/wasm.ts:473-476)."""

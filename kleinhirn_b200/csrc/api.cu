@@ -24,6 +24,9 @@ struct kh_plan {
   kh::CompiledPlan cp;
   kh::Exec ex;
   std::vector<int32_t> htable;
+  bool markers_ready = false;   // kh_upload_markers since creation (plans with a markers input)
+  void* d_capture = nullptr;    // capture slots (owned by ex once allocated)
+  std::vector<int32_t> qtypes;  // Julia type of each sequence of the batch
 };
 
 struct kh_bulk {
@@ -341,6 +344,47 @@ static void plan_prepare(kh_plan* plan, int rows) {
   ex.seq = rebase(offs, ex.d_table);
   ex.row_seq = ex.d_table + (intptr_t)offs.row_pos + T;
   ex.T = int(T);
+  if (!cp.in_markers.empty() && !plan->markers_ready) throw kh::ArgError("plan needs packedMarkers");
+  if (cp.rs_table) {
+    // the type row of each sequence, copied before the first op (src/plan/executor.ts:236-246)
+    char* dst = (char*)ex.buf(cp.buf_index.at(cp.rs_dst));
+    for (int b = 0; b < B; ++b) {
+      const int q = b < int(plan->qtypes.size()) ? plan->qtypes[size_t(b)] : 0;
+      KH_CUDA(cudaMemcpyAsync(dst + int64_t(b) * cp.rs_row_bytes, (const char*)cp.rs_table + int64_t(q) * cp.rs_row_bytes,
+                              size_t(cp.rs_row_bytes), cudaMemcpyDeviceToDevice, plan->owner->c->stream));
+    }
+  }
+}
+
+int kh_upload_markers(kh_plan* plan, const uint32_t* packed, size_t packed_len, const int32_t* qtypes,
+                      size_t n_qtypes) {
+  if (!plan || (packed_len && !packed) || (n_qtypes && !qtypes)) {
+    g_err = "kh_upload_markers: null argument";
+    return KH_ERR_ARG;
+  }
+  Ctx* c = plan->owner->c.get();
+  return guard(c, Latch::Yes, [&] {
+    const kh::CompiledPlan& cp = plan->cp;
+    if (cp.in_markers.empty()) throw kh::ArgError("kh_upload_markers: the plan has no markers input");
+    const int ib = cp.buf_index.at(cp.in_markers);
+    const size_t room = cp.bufs[size_t(ib)].fixed_bytes / 4;
+    if (packed_len > room)
+      throw kh::ArgError("kh_upload_markers: " + std::to_string(packed_len) + " words, the plan's payload holds " +
+                         std::to_string(room));
+    std::vector<int32_t> q(size_t(cp.batch), 0);
+    // (a plan without type rows ignores qtype, as the reference does)
+    for (size_t b = 0; cp.rs_table && b < n_qtypes && b < q.size(); ++b) {
+      if (qtypes[b] < 0 || qtypes[b] >= cp.rs_table_rows)
+        throw kh::ArgError("kh_upload_markers: qtype " + std::to_string(qtypes[b]) + " outside the " +
+                           std::to_string(cp.rs_table_rows) + " rows of the type table");
+      q[b] = qtypes[b];
+    }
+    if (packed_len)
+      KH_CUDA(cudaMemcpyAsync(plan->ex.buf(ib), packed, packed_len * 4, cudaMemcpyHostToDevice, c->stream));
+    KH_CUDA(cudaStreamSynchronize(c->stream));  // the caller may reuse its arrays at once
+    plan->qtypes = std::move(q);
+    plan->markers_ready = true;
+  });
 }
 
 int kh_run(kh_plan* plan, int rows) {
@@ -369,6 +413,58 @@ int kh_read_output(kh_plan* plan, float* out, size_t n) {
     if (n < need) throw kh::ArgError("kh_read_output: room for " + std::to_string(n) + " values, the output has " +
                                      std::to_string(need));
     KH_CUDA(cudaMemcpyAsync(out, plan->ex.d_out, need * 4, cudaMemcpyDeviceToHost, c->stream));
+    KH_CUDA(cudaStreamSynchronize(c->stream));
+    check_pipelines();
+  });
+}
+
+int kh_capture_check(const kh_plan* plan) {
+  if (!plan) {
+    g_err = "kh_capture_check: null plan";
+    return KH_ERR_ARG;
+  }
+  if (plan->cp.capturable) return KH_OK;
+  g_err = plan->cp.capture_refusal;
+  return KH_ERR_ARG;
+}
+
+int kh_run_capture(kh_plan* plan) {
+  if (!plan) {
+    g_err = "kh_run_capture: null plan";
+    return KH_ERR_ARG;
+  }
+  Ctx* c = plan->owner->c.get();
+  return guard(c, Latch::Yes, [&] {
+    const kh::CompiledPlan& cp = plan->cp;
+    if (!cp.capturable) throw kh::ArgError(cp.capture_refusal);
+    const size_t bytes = size_t(cp.capture_slots) * size_t(cp.capture_slot_bytes);
+    if (!plan->d_capture && bytes) {
+      KH_CUDA(cudaMalloc(&plan->d_capture, bytes));
+      plan->ex.owned.push_back(plan->d_capture);
+      KH_CUDA(cudaMemsetAsync(plan->d_capture, 0, bytes, c->stream));
+    }
+    plan_prepare(plan, cp.length);  // capture keeps the full bucket (src/plan/executor.ts:232)
+    kh::exec_capture(plan->ex, plan->d_capture, c->stream);
+    kh::exec_output(plan->ex, cp.out_rows, plan->ex.d_out, c->stream);
+    KH_CUDA(cudaGetLastError());
+  });
+}
+
+int kh_read_capture(kh_plan* plan, float* out, size_t n) {
+  if (!plan || !out) {
+    g_err = "kh_read_capture: null argument";
+    return KH_ERR_ARG;
+  }
+  Ctx* c = plan->owner->c.get();
+  return guard(c, Latch::Yes, [&] {
+    const kh::CompiledPlan& cp = plan->cp;
+    if (!cp.capturable) throw kh::ArgError(cp.capture_refusal);
+    const size_t need = size_t(cp.capture_slots) * size_t(cp.capture_slot_bytes) / 4;
+    if (n < need)
+      throw kh::ArgError("kh_read_capture: room for " + std::to_string(n) + " values, the capture has " +
+                         std::to_string(need));
+    if (!plan->d_capture) throw kh::ArgError("kh_read_capture: no capture run yet");
+    KH_CUDA(cudaMemcpyAsync(out, plan->d_capture, need * 4, cudaMemcpyDeviceToHost, c->stream));
     KH_CUDA(cudaStreamSynchronize(c->stream));
     check_pipelines();
   });
@@ -486,6 +582,8 @@ int kh_bulk_create(kh_plan* plan, int64_t max_tokens, int max_seqs, int64_t chun
   const int st = guard(c, Latch::No, [&] {
     const kh::CompiledPlan& cp = plan->cp;
     if (max_tokens < 1 || max_seqs < 1) throw kh::ArgError("kh_bulk_create: max_tokens and max_seqs must be >= 1");
+    if (!cp.in_markers.empty() || cp.rs_table)
+      throw kh::ArgError("kh_bulk_create: marker plans (GLiNER2, Julia) run through kh_upload_markers / kh_run");
     if (chunk_tokens < cp.length)
       throw kh::ArgError("kh_bulk_create: chunk_tokens " + std::to_string(chunk_tokens) +
                          " below the plan length " + std::to_string(cp.length));

@@ -364,13 +364,28 @@ __global__ void pool_kernel(const T* __restrict__ x, const float* __restrict__ m
 
 template <typename T>
 __global__ void gather_kernel(const T* __restrict__ x, T* __restrict__ out, int D, const int32_t* __restrict__ start,
-                              const uint32_t* __restrict__ markers, int K, int S) {
+                              const int32_t* __restrict__ len, const uint32_t* __restrict__ markers, int K, int S) {
   const int g = blockIdx.x;  // output row
   const int s = g / K;
   if (s >= S) return;
-  const int local = markers ? int(markers[s * 3 * K + (g - s * K)]) : 0;
-  const int64_t row = int64_t(start[s]) + local;
-  for (int d = threadIdx.x; d < D; d += blockDim.x) st(out, int64_t(g) * D + d, ld(x, row * D + d));
+  const uint32_t local = markers ? markers[s * 3 * K + (g - s * K)] : 0u;
+  // a marker past the rows this call computed reads zeros (the reference reads whatever that
+  // row of its buffer last held)
+  const bool ok = local < uint32_t(len[s]);
+  const int64_t row = int64_t(start[s]) + (ok ? local : 0);
+  for (int d = threadIdx.x; d < D; d += blockDim.x) st(out, int64_t(g) * D + d, ok ? ld(x, row * D + d) : 0.f);
+}
+
+// logits[k] = raw[k] / temp where the marker's mask word (f32 bits) is above 0.5, else -1e4;
+// the payload holds 3 K words per sequence: indices, mask, groups (src/kernels/masklogits.wgsl).
+template <typename T>
+__global__ void masklogits_kernel(const T* __restrict__ raw, const uint32_t* __restrict__ packed,
+                                  float* __restrict__ logits, int K, float temp, int total) {
+  const int k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= total) return;
+  const int b = k / K;
+  const float m = __uint_as_float(packed[b * 3 * K + K + (k - b * K)]);
+  logits[k] = m > 0.5f ? ld(raw, k) / temp : -1e4f;
 }
 
 template <typename T>
@@ -638,8 +653,22 @@ void launch_gather(bool f16, const void* x, void* out, int D, const SeqTable& se
                    cudaStream_t st) {
   if (seq.count <= 0) return;
   const int grid = seq.count * K;
-  if (f16) gather_kernel<__half><<<grid, 128, 0, st>>>((const __half*)x, (__half*)out, D, seq.start, markers, K, seq.count);
-  else gather_kernel<float><<<grid, 128, 0, st>>>((const float*)x, (float*)out, D, seq.start, markers, K, seq.count);
+  if (f16)
+    gather_kernel<__half><<<grid, 128, 0, st>>>((const __half*)x, (__half*)out, D, seq.start, seq.len, markers, K,
+                                                seq.count);
+  else
+    gather_kernel<float><<<grid, 128, 0, st>>>((const float*)x, (float*)out, D, seq.start, seq.len, markers, K,
+                                               seq.count);
+}
+
+void launch_masklogits(bool f16, const void* raw, const uint32_t* packed, float* logits, int K, float temp,
+                       int n_seqs, cudaStream_t st) {
+  const int total = n_seqs * K;
+  if (total <= 0) return;
+  if (f16)
+    masklogits_kernel<__half><<<(total + 127) / 128, 128, 0, st>>>((const __half*)raw, packed, logits, K, temp, total);
+  else
+    masklogits_kernel<float><<<(total + 127) / 128, 128, 0, st>>>((const float*)raw, packed, logits, K, temp, total);
 }
 
 void launch_im2col(bool f16, const void* x, const float* mask, void* out, int N, int KS, int rows, const SeqTable& seq,

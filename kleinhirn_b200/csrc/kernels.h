@@ -59,6 +59,9 @@ void launch_pool(bool f16, const void* x, const float* mask, void* out, int N, i
 // gather.wgsl with the zero marker buffer: out[s] = x[start[s] + marker[s]] (CLS row: marker 0).
 void launch_gather(bool f16, const void* x, void* out, int D, const SeqTable& seq, const uint32_t* markers,
                    int K, cudaStream_t st);
+// GLiNER2 / Julia logits: raw / temp where the marker is valid, -1e4 elsewhere (f32 out).
+void launch_masklogits(bool f16, const void* raw, const uint32_t* packed, float* logits, int K, float temp,
+                       int n_seqs, cudaStream_t st);
 
 // im2col.wgsl (DeBERTa-v2 convolution input).
 void launch_im2col(bool f16, const void* x, const float* mask, void* out, int N, int KS, int rows,

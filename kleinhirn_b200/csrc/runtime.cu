@@ -167,7 +167,7 @@ bool match_attention(const std::vector<const Json*>& ops, size_t i, AttnGroup& g
 
 const char* SUPPORTED[] = {"matmul", "mmtile", "mmtile8", "mmtile16", "layernorm", "embln", "add", "gather",
                            "pool", "geglu", "rope", "im2col", "attscore", "attsoftmax", "attpv", "attrel",
-                           "attsoftrel", "mbattention", "mbflash", "attention"};
+                           "attsoftrel", "mbattention", "mbflash", "attention", "masklogits"};
 
 }  // namespace
 
@@ -187,8 +187,10 @@ void plan_check(Ctx* ctx, const Json& plan) {
         throw PlanError("plan op " + op["name"].as_str() + ": head dimension above 64");
     }
   }
-  if (plan.has("rowSelect") && plan["rowSelect"].kind != Json::Null)
-    throw PlanError("rowSelect (Julia type rows) is not planned here");
+  if (plan.has("rowSelect") && plan["rowSelect"].kind != Json::Null) {
+    const Json& rs = plan["rowSelect"];
+    if (!is_weight(rs["table"].as_str())) throw PlanError("rowSelect: the table is not a weight");
+  }
 }
 
 void plan_compile(Ctx* ctx, const Json& plan, CompiledPlan& cp) {
@@ -200,9 +202,32 @@ void plan_compile(Ctx* ctx, const Json& plan, CompiledPlan& cp) {
   const bool f16 = cp.f16;
   const size_t esz = f16 ? 2 : 4;
 
+  // The ops in order, with their segment; the captureOps of capturable plans are compiled too,
+  // into launches only capture runs make.
+  if (f16) cp.capture_refusal = "capture needs an f32 plan: the capture copies and readCapture are f32";
+  else if (cp.batch != 1)
+    cp.capture_refusal = "capture needs a plan of batch 1, this one has " + std::to_string(cp.batch);
+  cp.capturable = cp.capture_refusal.empty();
   std::vector<const Json*> ops;
-  for (const Json& seg : plan["segments"].arr)
-    for (const Json& op : seg["ops"].arr) ops.push_back(&op);
+  std::vector<int> op_seg;
+  std::vector<bool> op_cap;
+  {
+    int sgi = 0;
+    for (const Json& seg : plan["segments"].arr) {
+      if (cp.capturable && seg.has("captureOps"))
+        for (const Json& op : seg["captureOps"].arr) {
+          ops.push_back(&op);
+          op_seg.push_back(sgi);
+          op_cap.push_back(true);
+        }
+      for (const Json& op : seg["ops"].arr) {
+        ops.push_back(&op);
+        op_seg.push_back(sgi);
+        op_cap.push_back(false);
+      }
+      ++sgi;
+    }
+  }
 
   // Buffers: declared ones, with their init blobs.
   std::map<std::string, const Json*> decl;
@@ -211,10 +236,20 @@ void plan_compile(Ctx* ctx, const Json& plan, CompiledPlan& cp) {
   cp.in_emb = inputs["embeddings"].as_str();
   cp.in_mask = inputs["mask"].as_str();
   cp.in_type = inputs.has("typeIds") ? inputs["typeIds"].as_str() : "";
+  cp.in_markers = inputs.has("markers") ? inputs["markers"].as_str() : "";
   const Json& out = plan["output"];
   cp.out_buf = out["buffer"].as_str();
   cp.out_rows = int(out["rows"].as_int());
   cp.out_cols = int(out["cols"].as_int());
+  cp.out_f32 = out.has("dtype") && out["dtype"].as_str() == "f32";
+  if (plan.has("rowSelect") && plan["rowSelect"].kind != Json::Null) {
+    const Json& rs = plan["rowSelect"];
+    const DevTensor& t = ctx->weight(rs["table"].as_str().substr(2), f16);
+    cp.rs_table = t.ptr;
+    cp.rs_row_bytes = int(rs["rowBytes"].as_int());
+    cp.rs_table_rows = int64_t(t.bytes / size_t(cp.rs_row_bytes));
+    cp.rs_dst = rs["dst"].as_str();
+  }
 
   std::map<std::string, BufInfo> info;
   auto touch = [&](const std::string& id) -> BufInfo& {
@@ -265,8 +300,17 @@ void plan_compile(Ctx* ctx, const Json& plan, CompiledPlan& cp) {
     std::string label;
     std::vector<std::string> names;
     std::function<Step(const CompiledPlan&)> make;
+    int seg = 0;
+    bool cap = false;
   };
   std::vector<Proto> protos;
+  size_t tagged = 0;  // protos whose segment is recorded
+  auto tag = [&](size_t op_index) {
+    for (; tagged < protos.size(); ++tagged) {
+      protos[tagged].seg = op_seg[op_index];
+      protos[tagged].cap = op_cap[op_index];
+    }
+  };
   auto bi = [](const CompiledPlan& c, const std::string& id) -> int {
     auto it = c.buf_index.find(id);
     if (it == c.buf_index.end()) throw PlanError("plan: buffer " + id + " has no memory");
@@ -303,8 +347,11 @@ void plan_compile(Ctx* ctx, const Json& plan, CompiledPlan& cp) {
   };
 
   std::vector<bool> consumed(ops.size(), false);
+  size_t last_op = 0;
   for (size_t i = 0; i < ops.size(); ++i) {
     if (consumed[i]) continue;
+    tag(last_op);
+    last_op = i;
     const Json& op = *ops[i];
     const std::string k = op["kernel"].as_str();
     const std::string name = op["name"].as_str();
@@ -574,6 +621,23 @@ void plan_compile(Ctx* ctx, const Json& plan, CompiledPlan& cp) {
       }});
       continue;
     }
+    if (k == "masklogits") {
+      const int K = cint(op, "K");
+      const float temp = float(cnum(op, "TEMP"));
+      const std::string raw = bind(op, 0), pk = bind(op, 1), o = bind(op, 2);
+      touch(o).elem = 4;  // f32 logits whatever the plan's storage type
+      protos.push_back({"masklogits", {name}, [=](const CompiledPlan& c) {
+        const int ir = bi(c, raw), ip = bi(c, pk), io = bi(c, o);
+        Step s;
+        s.run = [=](Exec& ex, cudaStream_t st) {
+          if (ex.bulk) throw PlanError("marker logits have no bulk form");
+          launch_masklogits(f16, ex.buf(ir), (const uint32_t*)ex.buf(ip), (float*)ex.buf(io), K, temp, ex.seq.count,
+                            st);
+        };
+        return s;
+      }});
+      continue;
+    }
     if (k == "im2col") {
       const int N = cint(op, "N"), KS = cint(op, "KS");
       const std::string x = bind(op, 0), m = bind(op, 1), o = bind(op, 2);
@@ -590,6 +654,21 @@ void plan_compile(Ctx* ctx, const Json& plan, CompiledPlan& cp) {
     throw PlanError("plan op " + name + ": kernel " + k + " outside an attention group has no CUDA computation");
   }
 
+  if (!ops.empty()) tag(last_op);
+  // Capture buffers (only read by the copies).
+  std::vector<std::vector<std::pair<std::string, int>>> seg_caps;
+  if (cp.capturable) {
+    for (const Json& seg : plan["segments"].arr) {
+      seg_caps.emplace_back();
+      if (!seg.has("capture")) continue;
+      for (const Json& c : seg["capture"].arr) {
+        use(c["buffer"].as_str());
+        seg_caps.back().emplace_back(c["buffer"].as_str(), int(c["slot"].as_int()));
+      }
+    }
+    cp.capture_slots = plan.has("captureSlots") ? int(plan["captureSlots"].as_int()) : 0;
+    cp.capture_slot_bytes = plan.has("captureSlotBytes") ? plan["captureSlotBytes"].as_int() : 0;
+  }
   // Output buffer must exist.
   touch(cp.out_buf);
   // Order buffers deterministically: declaration order.
@@ -612,14 +691,41 @@ void plan_compile(Ctx* ctx, const Json& plan, CompiledPlan& cp) {
       cp.buf_index[kv.first] = int(cp.bufs.size());
       cp.bufs.push_back(kv.second);
     }
+  if (!cp.in_markers.empty() && !cp.buf_index.count(cp.in_markers))
+    throw PlanError("plan: the marker input " + cp.in_markers + " is not read");
+  if (!cp.rs_dst.empty() && !cp.buf_index.count(cp.rs_dst)) throw PlanError("rowSelect: buffer " + cp.rs_dst + " is not used");
   const BufInfo& ob = cp.bufs[cp.buf_index.at(cp.out_buf)];
   cp.out_per_seq = ob.kind == BufInfo::Seqs;
   cp.tile_q = attention_tile_q(cp.f16);
+  // capture_order[0] launches nothing (copies of segments before any launch); entry k + 1 is
+  // proto k
+  if (cp.capturable) cp.capture_order.emplace_back();
   for (auto& p : protos) {
     Step s = p.make(cp);
     s.label = p.label;
     s.ops = p.names;
-    cp.steps.push_back(std::move(s));
+    CompiledPlan::CaptureEntry e;
+    if (p.cap) {
+      e.extra = int(cp.capture_steps.size());
+      cp.capture_steps.push_back(std::move(s));
+    } else {
+      e.step = int(cp.steps.size());
+      cp.steps.push_back(std::move(s));
+    }
+    if (cp.capturable) cp.capture_order.push_back(e);
+  }
+  if (cp.capturable) {
+    // a segment's copies follow its last launch (or the last launch before it)
+    for (size_t sgi = 0; sgi < seg_caps.size(); ++sgi) {
+      if (seg_caps[sgi].empty()) continue;
+      int at = 0;
+      for (size_t k = 0; k < protos.size(); ++k)
+        if (protos[k].seg <= int(sgi)) at = int(k) + 1;
+      for (const auto& bc : seg_caps[sgi]) {
+        if (bc.second < 0 || bc.second >= cp.capture_slots) throw PlanError("capture slot outside captureSlots");
+        cp.capture_order[size_t(at)].copies.emplace_back(cp.buf_index.at(bc.first), bc.second);
+      }
+    }
   }
 }
 
@@ -644,6 +750,7 @@ void exec_alloc(Exec& ex, Ctx* ctx, const CompiledPlan* cp, int64_t cap_rows, in
     if (!b.init.empty()) KH_CUDA(cudaMemcpyAsync(p, b.init.data(), b.init.size(), cudaMemcpyHostToDevice, ctx->stream));
     ex.owned.push_back(p);
     ex.ptr[i] = p;
+    ex.sizes.push_back(bytes);
     ex.bytes += int64_t(bytes);
   }
   const int64_t out_rows = std::max<int64_t>(cp->out_per_seq ? cap_seqs : cap_rows, bulk ? 0 : cp->out_rows);
@@ -716,6 +823,22 @@ void exec_steps(Exec& ex, cudaStream_t st) {
   for (const Step& s : ex.cp->steps) s.run(ex, st);
 }
 
+void exec_capture(Exec& ex, void* dst, cudaStream_t st) {
+  const CompiledPlan& cp = *ex.cp;
+  if (!cp.capturable) throw PlanError(cp.capture_refusal);
+  const size_t slot_bytes = size_t(cp.capture_slot_bytes);
+  for (const auto& e : cp.capture_order) {
+    if (e.step >= 0) cp.steps[size_t(e.step)].run(ex, st);
+    else if (e.extra >= 0) cp.capture_steps[size_t(e.extra)].run(ex, st);
+    for (const auto& c : e.copies) {
+      // copyBufferToBuffer(buffer, 0, capture, slot * slotBytes, slotBytes)
+      const size_t n = std::min(slot_bytes, ex.sizes[size_t(c.first)]);
+      KH_CUDA(cudaMemcpyAsync((char*)dst + size_t(c.second) * slot_bytes, ex.buf(c.first), n,
+                              cudaMemcpyDeviceToDevice, st));
+    }
+  }
+}
+
 namespace {
 template <typename T>
 __global__ void to_f32_kernel(const T* src, float* dst, int64_t n);
@@ -737,7 +860,7 @@ void exec_output(Exec& ex, int rows_out, float* dst, cudaStream_t st) {
   if (n <= 0) return;
   const void* src = ex.buf(ex.cp->buf_index.at(ex.cp->out_buf));
   int grid = int(std::min<int64_t>((n + 255) / 256, 4096));
-  if (ex.cp->f16) to_f32_kernel<__half><<<grid, 256, 0, st>>>((const __half*)src, dst, n);
+  if (ex.cp->f16 && !ex.cp->out_f32) to_f32_kernel<__half><<<grid, 256, 0, st>>>((const __half*)src, dst, n);
   else to_f32_kernel<float><<<grid, 256, 0, st>>>((const float*)src, dst, n);
 }
 

@@ -85,8 +85,30 @@ struct CompiledPlan {
   std::map<std::string, int> buf_index;
   std::vector<Step> steps;
   std::string in_emb, in_mask, in_type;  // input buffer ids ("" when absent)
+  std::string in_markers;                // marker payload of GLiNER2 / Julia plans ("" when absent)
+  // Julia type rows (src/plan/ir.ts:52, src/plan/executor.ts:236-246): before the first op,
+  // row qtype[b] of the table (in the plan's precision) is copied to row b of rs_dst.
+  const void* rs_table = nullptr;
+  int64_t rs_table_rows = 0;
+  int rs_row_bytes = 0;
+  std::string rs_dst;
   std::string out_buf;
   int out_rows = 0, out_cols = 0;
+  bool out_f32 = false;     // output dtype 'f32' (marker logits), else the plan's storage type
+  // Capture runs (src/plan/executor.ts:178-186, :267-281): f32 plans of batch 1 only. The
+  // capture launch list interleaves the plan steps with the launches of each segment's
+  // captureOps; after an entry, its copies put buffer prefixes into their slots.
+  struct CaptureEntry {
+    int step = -1;   // index into steps, or
+    int extra = -1;  // index into capture_steps
+    std::vector<std::pair<int, int>> copies;  // (buffer index, slot)
+  };
+  bool capturable = false;
+  std::string capture_refusal;  // why not, in the reference's words
+  std::vector<Step> capture_steps;
+  std::vector<CaptureEntry> capture_order;
+  int capture_slots = 0;
+  int64_t capture_slot_bytes = 0;
   bool out_per_seq = true;  // pooled head: one output row per sequence
   int tile_q = 64;          // attention query tile of the launch list
 };
@@ -99,6 +121,7 @@ struct Exec {
   int64_t cap_rows = 0;
   int cap_seqs = 0;
   std::vector<void*> ptr;       // by buffer index (inputs may point into bulk storage)
+  std::vector<size_t> sizes;    // allocated bytes, by buffer index
   std::vector<void*> owned;     // allocations to free
   bool bulk = false;            // ragged bulk execution (fixed-dispatch ops run once per sequence)
   // current launch
@@ -122,6 +145,10 @@ void plan_check(Ctx* ctx, const Json& plan);
 void build_seq_table(const std::vector<int32_t>& lens, int tile_q, std::vector<int32_t>& out, SeqTable& offsets,
                      int64_t& total_rows);
 void exec_steps(Exec& ex, cudaStream_t st);
+// A capture run (f32 plans of batch 1): the launches of exec_steps with each segment's
+// captureOps in place, and after each segment its capture buffers' first captureSlotBytes
+// copied into slot * captureSlotBytes of `dst` (device memory of captureSlots slots).
+void exec_capture(Exec& ex, void* dst, cudaStream_t st);
 void exec_output(Exec& ex, int rows_out, float* dst, cudaStream_t st);
 
 }  // namespace kh

@@ -214,6 +214,8 @@ class OraclePlan:
         ops = fuse_attention([op for s in plan["segments"] for op in s["ops"]])
         used = {b for o in ops for b in o["bind"]} | {plan["output"]["buffer"]} | \
             {v for v in plan["inputs"].values() if isinstance(v, str)}
+        if plan.get("rowSelect"):  # src/plan/wasm.ts:291
+            used.add(plan["rowSelect"]["dst"])
         self.bufs: dict[str, tuple[int, int]] = {}
         for d in plan["buffers"]:
             if d["id"] not in used:
@@ -314,8 +316,9 @@ class OraclePlan:
         p, n = self.bufs[bid]
         return self.rt.f32(p, n // 4)
 
-    def upload(self, embeddings: np.ndarray, mask: np.ndarray, type_ids: np.ndarray | None = None) -> None:
-        """src/plan/wasm.ts:409-440 (f32 word rows only)."""
+    def upload(self, embeddings: np.ndarray, mask: np.ndarray, type_ids: np.ndarray | None = None,
+               packed_markers: np.ndarray | None = None, qtype=None) -> None:
+        """src/plan/wasm.ts:409-440 (f32 word rows only): inputs, marker payload, Julia type rows."""
         i = self.plan["inputs"]
 
         def put(bid, src: np.ndarray):
@@ -328,10 +331,21 @@ class OraclePlan:
             raise ValueError("the WASM executor takes f32 word rows")
         put(i["embeddings"], embeddings)
         put(i["mask"], mask.astype(np.float32))
+        if i.get("markers"):
+            if packed_markers is None:
+                raise ValueError("plan needs packedMarkers")
+            put(i["markers"], np.asarray(packed_markers, dtype=np.uint32))
         if i.get("typeIds"):
             if type_ids is None:
                 raise ValueError("plan needs typeIds")
             put(i["typeIds"], type_ids.astype(np.uint32))
+        rs = self.plan.get("rowSelect")
+        if rs:
+            qtypes = list(qtype) if isinstance(qtype, (list, tuple, np.ndarray)) else [qtype or 0]
+            table, dst, rb = self._at(rs["table"]), self._at(rs["dst"]), rs["rowBytes"]
+            for b in range(self.batch):
+                q = int(qtypes[b]) if b < len(qtypes) else 0
+                self.rt.mem[dst + b * rb: dst + (b + 1) * rb] = self.rt.mem[table + q * rb: table + (q + 1) * rb]
 
     def run(self, rows: int) -> None:
         if rows < 1 or rows > self.length * self.batch:
