@@ -12,21 +12,24 @@
 // Work: one CTA per (packed tile of 128 consecutive packed rows, group of HG heads). Short
 // sequences share a tile; a pair of rows from different sequences is masked. The keys of a tile
 // are the packed rows of every sequence its rows belong to (clamped to +-WINDOW around the tile
-// on windowed layers), in tiles of 128; which of them are present and unmasked is computed once
-// per CTA as bit masks. The CTA walks (head, key tile) items in order, 320 threads:
-//   warp 0     TMA: Q of each head, K and V of each item, into rings that run ahead across heads;
-//   warp 1     one thread issues S = Q K^T (M 128, N 128 keys, K = D) into TMEM columns
-//              [0, 128) and O += P V (M 128, N = D, K 128 keys, V as an MN-major operand) into
-//              the head's O buffer, TMEM columns [128 + D (h % 2), 128 + D (h % 2) + D): O
-//              accumulates over the key tiles of a head in TMEM; the next item's S is issued as
-//              soon as the softmax has read the current one, before the current PV;
-//   warps 2-9  softmax, two threads per query row (TMEM lane), warps 2-5 on keys [0, 64) of
-//              each key tile and warps 6-9 on keys [64, 128): the scores in registers, the
-//              exponentials exp2(s - m) in the log2 domain against a reference point m that
-//              only moves when a tile's maximum exceeds it by more than 8 (then O is rescaled
-//              in TMEM, which is rare), P in f16 into shared memory (128-byte swizzled K-major
-//              rows); the two threads of a row exchange their maxima per item and their sums
-//              per head through shared memory; at the end of a head, ctx = O / sum.
+// on windowed layers), in tiles of 64; which of them are present and unmasked is computed once
+// per CTA as bit masks. The work is (head, key tile) items on two streams: stream 0 takes the
+// even heads of the CTA, stream 1 the odd ones, and their items alternate on the tensor core so
+// each stream's softmax runs while the other's products do. With one head per CTA (small
+// launches) the two streams split the head's key tiles and combine their partial results (split
+// mode). 320 threads:
+//   warp 0     TMA: Q of each head into its stream's slot, K and V of each item (64 rows) into
+//              rings that run ahead across items;
+//   warp 1     one thread issues S = Q K^T (M 128, N 64 keys, K = D) into the stream's TMEM
+//              columns [64 g, 64 g + 64), two items ahead, and O += P V (M 128, N = D, K 64 keys,
+//              V as an MN-major operand) into the stream's O columns [128 + D g, 128 + D g + D),
+//              which accumulate over the key tiles of a head;
+//   warps 2-9  softmax, warps 2-5 stream 0 and 6-9 stream 1, one thread per query row (TMEM
+//              lane): the 64 scores in registers, the exponentials exp2(s - m) in the log2
+//              domain against a reference point m that only moves when a tile's maximum exceeds
+//              it by more than 8 (then O is rescaled in TMEM, which is rare), P in f16 into the
+//              stream's shared-memory block (128-byte swizzled K-major rows); at the end of a
+//              head, ctx = O / sum.
 // Two CTAs share an SM (256 TMEM columns and <= 108 KB of shared memory each).
 
 #include <algorithm>
@@ -45,30 +48,30 @@ namespace {
 using namespace sm100;
 
 constexpr int TQ = 128;
-constexpr int TKEYS = 128;
-constexpr int THREADS = 320;  // producer warp, MMA warp, 8 softmax warps (two per query row)
+constexpr int TK = 64;        // keys per item
+constexpr int THREADS = 320;  // producer warp, MMA warp, two softmax warpgroups (one query row per thread)
 constexpr uint32_t TMEM_COLS = 256;
-constexpr int MAXKT = 160;  // key tiles of one CTA: sequences up to 10,000 rows
+constexpr int MAXKT = 320;  // key tiles of one CTA: sequences up to 20,480 rows
 
 template <int D>
 struct Cfg {
-  static constexpr int ROW_BYTES = D * 2;   // one q / k / v row: the swizzle width
-  static constexpr int TILE = 128 * ROW_BYTES;
-  static constexpr int QS = D == 32 ? 2 : 1;  // Q buffers
-  static constexpr int KS = 2;                // K stages
-  static constexpr int VS = D == 32 ? 2 : 1;  // V stages
-  static constexpr int Q_OFF = 0;
-  static constexpr int K_OFF = Q_OFF + QS * TILE;
-  static constexpr int V_OFF = K_OFF + KS * TILE;
-  static constexpr int P_OFF = V_OFF + VS * TILE;  // 2 blocks of 128 rows x 64 keys, 16 KB each
-  static constexpr int BITS_OFF = P_OFF + 32768;   // present-and-unmasked / masked-key bits
-  static constexpr int XCH_OFF = BITS_OFF + 2 * MAXKT * 4 * 4;  // row max / sum exchange of the two halves
+  static constexpr int ROW_BYTES = D * 2;     // one q / k / v row: the swizzle width
+  static constexpr int QTILE = TQ * ROW_BYTES;  // 128 query rows
+  static constexpr int KTILE = TK * ROW_BYTES;  // 64 key (or value) rows
+  static constexpr int KS = D == 32 ? 4 : 2;  // K stages
+  static constexpr int VS = D == 32 ? 4 : 2;  // V stages
+  static constexpr int Q_OFF = 0;             // one Q tile per stream
+  static constexpr int K_OFF = Q_OFF + 2 * QTILE;
+  static constexpr int V_OFF = K_OFF + KS * KTILE;
+  static constexpr int P_OFF = V_OFF + VS * KTILE;  // one P block per stream: 128 rows x 64 keys, 16 KB
+  static constexpr int BITS_OFF = P_OFF + 2 * 16384;  // present-and-unmasked key bits [tile][2]
   // D = 32: the row sums come from the tensor core (P times a ones tile, 16 columns of TMEM per
-  // head parity next to O); D = 64 has no TMEM room left and sums in the softmax threads.
+  // stream next to O); D = 64 has no TMEM room left and sums in the softmax threads.
   static constexpr bool SUMS = D == 32;
-  static constexpr int ONES_OFF = XCH_OFF + 2 * (4 * 2 * 2 * 128);  // xmax and xsum, f32 [2][2][128] each
-  static constexpr int BAR_OFF = ONES_OFF + (SUMS ? 4096 : 0);       // ones: 2 blocks of 16 rows x 64 keys
-  static constexpr int USED = BAR_OFF + 256;
+  static constexpr int XCH_OFF = BITS_OFF + MAXKT * 2 * 4;  // split mode: m and l of both streams, f32 [2][2][128]
+  static constexpr int ONES_OFF = XCH_OFF + 2 * 2 * 128 * 4;
+  static constexpr int BAR_OFF = ONES_OFF + (SUMS ? 2048 : 0);  // ones: 16 rows x 64 keys
+  static constexpr int USED = BAR_OFF + 512;
   // at least 100 KB so that no more than two CTAs (2 x 256 TMEM columns) share an SM
   static constexpr int SMEM = (USED + 1024 > 102400 ? USED + 1024 : 102400);
   static constexpr uint64_t LAYOUT = D == 64 ? 2ull : 4ull;  // 128- or 64-byte swizzle
@@ -97,8 +100,9 @@ __device__ __forceinline__ uint64_t desc_rows(const void* smem) {
   return ((addr >> 4) & 0x3FFFull) | (1ull << 16) | (Cfg<D>::SBO << 32) | (1ull << 46) | (Cfg<D>::LAYOUT << 61);
 }
 
-template <int D, bool REL = false>
-__global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_constant__ CUtensorMap tm, const Params p) {
+template <int D, bool REL = false, bool SPLIT = false>
+__global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_constant__ CUtensorMap tmq,
+                                                             const __grid_constant__ CUtensorMap tmkv, const Params p) {
   using C = Cfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -106,23 +110,20 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
   uint8_t* sK = smem + C::K_OFF;
   uint8_t* sV = smem + C::V_OFF;
   uint8_t* sP = smem + C::P_OFF;
-  uint32_t* vbits = reinterpret_cast<uint32_t*>(smem + C::BITS_OFF);  // [tile][4]: key present, unmasked
-  uint32_t* hbits = vbits + MAXKT * 4;                                 // [tile][4]: key present, masked
-  float* xmax = reinterpret_cast<float*>(smem + C::XCH_OFF);           // [parity][half][row]
-  float* xsum = xmax + 2 * 2 * 128;                                    // [parity][half][row]
+  uint32_t* vbits = reinterpret_cast<uint32_t*>(smem + C::BITS_OFF);  // [tile][2]: key present, unmasked
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
-  uint64_t* q_full = bars;       // 2
-  uint64_t* q_empty = bars + 2;  // 2
-  uint64_t* k_full = bars + 4;   // 2
-  uint64_t* k_empty = bars + 6;  // 2
-  uint64_t* v_full = bars + 8;   // 2
-  uint64_t* v_empty = bars + 10; // 2
-  uint64_t* s_full = bars + 12;
-  uint64_t* s_empty = bars + 13;
-  uint64_t* p_full = bars + 14;
-  uint64_t* o_full = bars + 15;
-  uint64_t* drain = bars + 16;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 17);
+  uint64_t* q_full = bars;             // [stream]
+  uint64_t* q_empty = bars + 2;        // [stream]
+  uint64_t* s_full = bars + 4;         // [stream]
+  uint64_t* s_empty = bars + 6;        // [stream]
+  uint64_t* p_full = bars + 8;         // [stream]
+  uint64_t* o_full = bars + 10;        // [stream]
+  uint64_t* drain = bars + 12;
+  uint64_t* k_full = bars + 13;        // [KS]
+  uint64_t* k_empty = k_full + C::KS;  // [KS]
+  uint64_t* v_full = k_empty + C::KS;  // [VS]
+  uint64_t* v_empty = v_full + C::VS;  // [VS]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(v_empty + C::VS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -134,31 +135,58 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
     kstart = max(kstart, q0 - p.window);
     kend = min(kend, q0 + TQ + p.window);
   }
-  const int nkt = min((kend - kstart + TKEYS - 1) / TKEYS, MAXKT);
+  const int nkt = min((kend - kstart + TK - 1) / TK, MAXKT);
   const int NI = HG * nkt;  // (head, key tile) items
+  // The items in the order the producer and the MMA warp take them: heads in pairs (2a, 2a + 1),
+  // the key tiles of the two alternating (stream 0 takes even heads, stream 1 odd ones); a last
+  // head without a partner runs alone on stream 0. With one head per CTA (split mode: small
+  // launches) the streams split the head's key tiles instead, stream g taking tiles j = g mod 2,
+  // and combine their partial softmax results at the end.
+  constexpr bool split = SPLIT;  // (launched with HG == 1)
+  auto advance = [HG, nkt](int& hh, int& j, int& g) {
+    if constexpr (split) {
+      ++j;
+      g ^= 1;
+    } else if (g == 0 && hh + 1 < HG) {
+      g = 1;
+      ++hh;
+    } else {
+      if (g == 1) --hh;
+      g = 0;
+      if (++j == nkt) {
+        j = 0;
+        hh += 2;
+      }
+    }
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < 2; ++s) {
       mbar_init(&q_full[s], 1);
       mbar_init(&q_empty[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_empty[s], 128);
+      mbar_init(&p_full[s], 128);
+      mbar_init(&o_full[s], 1);
+    }
+    for (int s = 0; s < C::KS; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < C::VS; ++s) {
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(s_empty, 256);
-    mbar_init(p_full, 256);
-    mbar_init(o_full, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
-    prefetch_tmap(&tm);
+    prefetch_tmap(&tmq);
+    prefetch_tmap(&tmkv);
   }
   if constexpr (C::SUMS) {
-    // B operand of the row-sum MMA: 16 x 128 f16 ones (every swizzle of it is the same)
+    // B operand of the row-sum MMA: 16 x 64 f16 ones (every swizzle of it is the same)
     uint4* ones = reinterpret_cast<uint4*>(smem + C::ONES_OFF);
-    for (int i = threadIdx.x; i < 4096 / 16; i += THREADS) ones[i] = make_uint4(0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);
+    for (int i = threadIdx.x; i < 2048 / 16; i += THREADS) ones[i] = make_uint4(0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);
     fence_proxy_async_smem();
   }
   if (warp == 1) tmem_alloc(tmem_holder, TMEM_COLS);
@@ -172,100 +200,109 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
       bool ok = true;
       // issued loads not yet known complete: parity per ring slot (bit 2 = issued)
       uint32_t pend_q = 0, pend_k = 0, pend_v = 0;
-      // (head, key tile) of item it, advanced without a division
-      int hh = 0, j = 0;
-      for (int it = 0; it < NI && ok; ++it, j = (j + 1 == nkt) ? (++hh, 0) : j + 1) {
+      int qn0 = 0, qn1 = 0;  // heads loaded per stream
+      int hh = 0, j = 0, g = 0;
+      for (int it = 0; it < NI && ok; ++it, advance(hh, j, g)) {
         const int h = hg0 + hh;
-        const int y = kstart + j * TKEYS;
-        if (j == 0) {
-          const int s = hh % C::QS;
-          const uint32_t u = uint32_t(hh / C::QS);
-          if (*abort_flag || !mbar_wait(&q_empty[s], (u & 1) ^ 1, 20)) { ok = false; break; }
-          mbar_arrive_expect_tx(&q_full[s], C::TILE);
-          tma_load_2d(sQ + s * C::TILE, &tm, &q_full[s], h * D, q0);
-          pend_q = (pend_q & ~(7u << (3 * s))) | ((4u | (u & 1)) << (3 * s));
+        const int y = kstart + j * TK;
+        if (split ? j < 2 : j == 0) {  // the stream's first item of the head: its Q tile
+          const uint32_t u = uint32_t(g ? qn1++ : qn0++);
+          if (*abort_flag || !mbar_wait(&q_empty[g], (u & 1) ^ 1, 20)) { ok = false; break; }
+          mbar_arrive_expect_tx(&q_full[g], C::QTILE);
+          tma_load_2d(sQ + g * C::QTILE, &tmq, &q_full[g], h * D, q0);
+          pend_q = (pend_q & ~(7u << (3 * g))) | ((4u | (u & 1)) << (3 * g));
         }
         {
           const int s = it % C::KS;
           const uint32_t u = uint32_t(it / C::KS);
           if (*abort_flag || !mbar_wait(&k_empty[s], (u & 1) ^ 1, 21)) { ok = false; break; }
-          mbar_arrive_expect_tx(&k_full[s], C::TILE);
-          tma_load_2d(sK + s * C::TILE, &tm, &k_full[s], (H + h) * D, y);
+          mbar_arrive_expect_tx(&k_full[s], C::KTILE);
+          tma_load_2d(sK + s * C::KTILE, &tmkv, &k_full[s], (H + h) * D, y);
           pend_k = (pend_k & ~(7u << (3 * s))) | ((4u | (u & 1)) << (3 * s));
         }
         {
           const int s = it % C::VS;
           const uint32_t u = uint32_t(it / C::VS);
           if (*abort_flag || !mbar_wait(&v_empty[s], (u & 1) ^ 1, 22)) { ok = false; break; }
-          mbar_arrive_expect_tx(&v_full[s], C::TILE);
-          tma_load_2d(sV + s * C::TILE, &tm, &v_full[s], (2 * H + h) * D, y);
+          mbar_arrive_expect_tx(&v_full[s], C::KTILE);
+          tma_load_2d(sV + s * C::KTILE, &tmkv, &v_full[s], (2 * H + h) * D, y);
           pend_v = (pend_v & ~(7u << (3 * s))) | ((4u | (u & 1)) << (3 * s));
         }
       }
       if (!ok) {
         *abort_flag = 1;
         // every copy this thread issued lands before the CTA ends
-        for (int s = 0; s < 2; ++s) {
+        for (int s = 0; s < 2; ++s)
           if ((pend_q >> (3 * s)) & 4u) mbar_wait(&q_full[s], (pend_q >> (3 * s)) & 1u, 31);
+        for (int s = 0; s < C::KS; ++s)
           if ((pend_k >> (3 * s)) & 4u) mbar_wait(&k_full[s], (pend_k >> (3 * s)) & 1u, 32);
+        for (int s = 0; s < C::VS; ++s)
           if ((pend_v >> (3 * s)) & 4u) mbar_wait(&v_full[s], (pend_v >> (3 * s)) & 1u, 33);
-        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc_s = idesc_f16(128, TKEYS);
+      const uint32_t idesc_s = idesc_f16(128, TK);
       const uint32_t idesc_o = idesc_f16(128, D) | (1u << 16);  // B (V) MN-major
       bool ok = true;
-      int sh = 0, sj = 0;  // (head, key tile) of the next S to issue
+      int sh = 0, sj = 0, sg = 0;   // (head, key tile, stream) of the next S to issue
+      int su0 = 0, su1 = 0, sq0 = 0, sq1 = 0;  // S issued / heads started per stream
       auto issue_s = [&](int it) -> bool {
-        const int hh = sh, j = sj;
-        sj = (sj + 1 == nkt) ? (++sh, 0) : sj + 1;
-        const int qs = hh % C::QS, ks = it % C::KS;
-        if (j == 0 && !mbar_wait(&q_full[qs], uint32_t(hh / C::QS) & 1, 23)) return false;
+        const int j = sj, g = sg;
+        const int u = g ? su1++ : su0++;
+        advance(sh, sj, sg);
+        const int ks = it % C::KS;
+        if (split ? j < 2 : j == 0) {
+          const int qu = g ? sq1++ : sq0++;
+          if (!mbar_wait(&q_full[g], uint32_t(qu) & 1, 23)) return false;
+        }
         if (*abort_flag || !mbar_wait(&k_full[ks], uint32_t(it / C::KS) & 1, 24)) return false;
-        if (*abort_flag || !mbar_wait(s_empty, uint32_t(it & 1) ^ 1, 25)) return false;
+        if (*abort_flag || !mbar_wait(&s_empty[g], (uint32_t(u) & 1) ^ 1, 25)) return false;
         fence_after_sync();
-        const uint64_t dq = desc_rows<D>(sQ + qs * C::TILE);
-        const uint64_t dk = desc_rows<D>(sK + ks * C::TILE);
+        const uint64_t dq = desc_rows<D>(sQ + g * C::QTILE);
+        const uint64_t dk = desc_rows<D>(sK + ks * C::KTILE);
 #pragma unroll
-        for (int k = 0; k < D / 16; ++k) mma_f16(tmem, dq + uint64_t(2 * k), dk + uint64_t(2 * k), idesc_s, k ? 1u : 0u);
-        mma_commit(s_full);
+        for (int k = 0; k < D / 16; ++k)
+          mma_f16(tmem + uint32_t(g * TK), dq + uint64_t(2 * k), dk + uint64_t(2 * k), idesc_s, k ? 1u : 0u);
+        mma_commit(&s_full[g]);
         mma_commit(&k_empty[ks]);
-        if (j == nkt - 1) mma_commit(&q_empty[qs]);
+        if (split ? j + 2 >= nkt : j == nkt - 1) mma_commit(&q_empty[g]);  // the stream's last item of the head
         return true;
       };
+      // S runs two items ahead of PV: the next item's S belongs to the other stream, the one
+      // after to this stream, whose softmax can then start on it while its PV runs.
       ok = NI > 0 && issue_s(0);
-      int hh = 0, j = 0;  // (head, key tile) of the PV product of item it
-      for (int it = 0; it < NI && ok; ++it, j = (j + 1 == nkt) ? (++hh, 0) : j + 1) {
-        if (it + 1 < NI && !issue_s(it + 1)) { ok = false; break; }
+      if (ok && NI > 1) ok = issue_s(1);
+      int hh = 0, j = 0, g = 0;
+      int pu0 = 0, pu1 = 0;
+      for (int it = 0; it < NI && ok; ++it, advance(hh, j, g)) {
+        if (it + 2 < NI && !issue_s(it + 2)) { ok = false; break; }
+        const int u = g ? pu1++ : pu0++;
         const int vs = it % C::VS;
-        if (*abort_flag || !mbar_wait(p_full, uint32_t(it & 1), 26) ||
+        if (*abort_flag || !mbar_wait(&p_full[g], uint32_t(u) & 1, 26) ||
             !mbar_wait(&v_full[vs], uint32_t(it / C::VS) & 1, 27)) {
           ok = false;
           break;
         }
         fence_after_sync();
-        // O of head hh accumulates over its key tiles, in the TMEM buffer of the head's parity
-        const uint32_t o_addr = tmem + 128 + uint32_t((hh & 1) * D);
-        const uint64_t dv = desc_rows<D>(sV + vs * C::TILE);
+        // O of the stream's head accumulates over its key tiles in the stream's TMEM buffer
+        const uint32_t o_addr = tmem + 128 + uint32_t(g * D);
+        const uint64_t dv = desc_rows<D>(sV + vs * C::KTILE);
+        const uint64_t dp = desc_rows<64>(sP + g * 16384);
+        const bool acc = split ? j >= 2 : j > 0;  // not the stream's first item of the head
 #pragma unroll
-        for (int kk = 0; kk < TKEYS / 16; ++kk) {
-          const uint64_t dp = desc_rows<64>(sP + (kk >> 2) * 16384) + uint64_t(2 * (kk & 3));
-          mma_f16(o_addr, dp, dv + uint64_t(2 * D * kk), idesc_o, (j | kk) ? 1u : 0u);
-        }
+        for (int kk = 0; kk < TK / 16; ++kk)
+          mma_f16(o_addr, dp + uint64_t(2 * kk), dv + uint64_t(2 * D * kk), idesc_o, (acc || kk) ? 1u : 0u);
         if constexpr (C::SUMS) {
           // row sums of P: P times the ones tile, accumulated like O
-          const uint32_t l_addr = tmem + 192 + uint32_t((hh & 1) * 16);
+          const uint32_t l_addr = tmem + 192 + uint32_t(g * 16);
           const uint32_t idesc_l = idesc_f16(128, 16);
+          const uint64_t d1 = desc_rows<64>(smem + C::ONES_OFF);
 #pragma unroll
-          for (int kk = 0; kk < TKEYS / 16; ++kk) {
-            const uint64_t dp = desc_rows<64>(sP + (kk >> 2) * 16384) + uint64_t(2 * (kk & 3));
-            const uint64_t d1 = desc_rows<64>(smem + C::ONES_OFF + (kk >> 2) * 2048) + uint64_t(2 * (kk & 3));
-            mma_f16(l_addr, dp, d1, idesc_l, (j | kk) ? 1u : 0u);
-          }
+          for (int kk = 0; kk < TK / 16; ++kk)
+            mma_f16(l_addr, dp + uint64_t(2 * kk), d1 + uint64_t(2 * kk), idesc_l, (acc || kk) ? 1u : 0u);
         }
-        mma_commit(o_full);
+        mma_commit(&o_full[g]);
         mma_commit(&v_empty[vs]);
       }
       if (!ok) {
@@ -275,27 +312,20 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
       }
     }
   } else {
-    // Two threads per query row: warps 2-5 take keys [0, 64) of every key tile, warps 6-9 keys
-    // [64, 128) (TMEM lanes follow warp % 4 in both). They agree on the row maximum through
-    // shared memory once per item and on the row sum once per head.
+    // Softmax: warps 2-5 run stream 0 (even heads of the CTA), warps 6-9 stream 1 (odd heads),
+    // one thread per query row (TMEM lane: warp % 4 gives the lane quarter) over the 64 keys of
+    // every item. The two streams alternate on the tensor core and cover each other's waits.
+    const int g = (warp - 2) >> 2;
     const int quarter = warp & 3;
-    const int hf = (warp - 2) >> 2;           // half of the key tile
-    const int r_local = quarter * 32 + lane;  // query row = TMEM lane
-    const int tid = threadIdx.x - 64;         // 0 .. 255
-    const int pair_bar = 1 + quarter;         // named barrier of the two warps of this quarter
-    // which key rows of every key tile are present and unmasked (computed once for all heads)
-    if (tid < 128) {
-      for (int j = 0; j < nkt; ++j) {
-        const int kk = kstart + j * TKEYS + tid;
-        const bool have = kk < kend && kk < p.T;
-        const bool valid = have && p.mask[kk] > 0.5f;
-        const uint32_t vb = __ballot_sync(0xffffffffu, valid);
-        const uint32_t hb = __ballot_sync(0xffffffffu, have && !valid);
-        if (lane == 0) {
-          vbits[j * 4 + (tid >> 5)] = vb;
-          hbits[j * 4 + (tid >> 5)] = hb;
-        }
-      }
+    const int r_local = quarter * 32 + lane;     // query row = TMEM lane
+    const int tid_g = ((warp - 2) & 3) * 32 + lane;  // 0 .. 127 within the stream
+    const int tid = threadIdx.x - 64;            // 0 .. 255
+    // which key rows of every key tile are present and unmasked (once for all heads)
+    for (int j = tid >> 6; j < nkt; j += 4) {
+      const int kk = kstart + j * TK + (tid & 63);
+      const bool valid = kk < kend && kk < p.T && p.mask[kk] > 0.5f;
+      const uint32_t vb = __ballot_sync(0xffffffffu, valid);
+      if (lane == 0) vbits[j * 2 + ((tid & 63) >> 5)] = vb;
     }
     const int row = q0 + r_local;
     const bool in_range = row < p.T;
@@ -314,49 +344,40 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
     }
     named_bar(5, 256);
     const uint32_t trow = tmem + (uint32_t(quarter * 32) << 16);
-    const int vrow = tid & 127, vpart = tid >> 7;  // value row (and its half) this thread clears
+    const uint32_t s_addr = trow + uint32_t(g * TK);
+    const uint32_t o_addr = trow + 128 + uint32_t(g * D);
+    const int vrow = tid_g & 63, vpart = tid_g >> 6;  // value row (and its half) this thread clears
     bool ok = true;
-    // Running state of the current head (the same in both threads of a row): m = the reference
-    // point of the exponentials (scaled log2 units); m only moves when a key tile's maximum
-    // exceeds it by more than 8 (probabilities stay <= 2^8, exact in f16 up to the rounding),
-    // and then O in TMEM is rescaled before the tile's PV product. l = this thread's part of the
-    // row sum.
-    bool started = false;
-    float m = 0.f, l = 0.f;
-    bool pending = false;  // the previous head's context is still to be written
-    float l_prev = 0.f;
     auto wwait = [&](uint64_t* bar, uint32_t parity, int code) -> bool {
       const bool r = !*abort_flag && mbar_wait(bar, parity, code);
       return __all_sync(0xffffffffu, r);
     };
-    // PV products observed complete so far. o_full completes once per PV, in order; the softmax
-    // observes every phase in order and has observed PV(it - 1) before it releases item it to
-    // the PV product, so the barrier is never two phases ahead of the phase waited for.
+    // PV products of this stream observed complete so far (o_full completes once per PV, in
+    // order; the softmax observes PV(u - 1) before it releases item u, so the barrier is never
+    // two phases ahead of the phase waited for)
     int o_done = 0;
-    auto wait_pv = [&](int it) -> bool {
-      while (o_done <= it) {
-        if (!wwait(o_full, uint32_t(o_done & 1), 43)) return false;
+    auto wait_pv = [&](int u) -> bool {
+      while (o_done <= u) {
+        if (!wwait(&o_full[g], uint32_t(o_done & 1), 43)) return false;
         ++o_done;
       }
       fence_after_sync();
       return true;
     };
-    // context row of head hh = O / l over this thread's D / 2 columns (a masked query row, or
-    // one without a kept key, is exactly zero: select, not multiply)
-    // (lt: the row sum of both halves; with tensor-core sums it is read from TMEM here)
+    // context row of head hh = O / l (a masked query row, or one without a kept key, is exactly
+    // zero: select, not multiply); with tensor-core sums l is read from TMEM
     auto finish_head = [&](int hh, float lt) {
       if constexpr (C::SUMS) {
         uint32_t lr[8];
-        tmem_ld8(trow + 192 + uint32_t((hh & 1) * 16), lr);
+        tmem_ld8(trow + 192 + uint32_t(g * 16), lr);
         tmem_ld_wait();
         lt = __uint_as_float(lr[0]);
       }
       const bool live = qvalid && lt > 0.f;
       const float inv = live ? 1.0f / lt : 0.f;
-      const uint32_t o_addr = trow + 128 + uint32_t((hh & 1) * D + hf * (D / 2));
-      uint4* dst = reinterpret_cast<uint4*>(p.ctx + int64_t(row) * H * D + int64_t(hg0 + hh) * D + hf * (D / 2));
+      uint4* dst = reinterpret_cast<uint4*>(p.ctx + int64_t(row) * H * D + int64_t(hg0 + hh) * D);
 #pragma unroll
-      for (int c = 0; c < D / 2; c += 8) {
+      for (int c = 0; c < D; c += 8) {
         uint32_t r[8];
         tmem_ld8(o_addr + c, r);
         tmem_ld_wait();
@@ -368,120 +389,107 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
         if (in_range) dst[c / 8] = *reinterpret_cast<uint4*>(hv);
       }
     };
-    int hh = 0, j = 0;  // (head, key tile) of item it
-    for (int it = 0; it < NI; ++it, j = (j + 1 == nkt) ? (++hh, 0) : j + 1) {
-      // A failed wait never ends one warp of a pair alone: the pair decides together at its
-      // named barriers (bar.red), so neither warp is left waiting at one.
-      bool fail = !ok;
-      if (j == 0 && it > 0) {
-        // a new head starts over; the previous one is written further down, once its last PV
-        // product is done (its O stays in the other TMEM buffer meanwhile)
-        pending = true;
-        l_prev = l;
-        started = false;
-        l = 0.f;
-      }
-      const int k0 = kstart + j * TKEYS + hf * 64;  // first key of this thread's half
-      const int clo = min(max(lo - k0, 0), 64), chi = min(max(hi - k0, 0), 64);
-      // keep masks of this thread's two 32-key chunks: in the row's key range, present, unmasked
-      uint32_t km[2];
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const int a = min(max(clo - 32 * c, 0), 32), b = min(max(chi - 32 * c, 0), 32);
-        const uint32_t below_b = b >= 32 ? 0xffffffffu : ((1u << b) - 1u);
-        const uint32_t below_a = a >= 32 ? 0xffffffffu : ((1u << a) - 1u);
-        km[c] = (below_b & ~below_a) & vbits[j * 4 + hf * 2 + c];
-      }
-      if (!fail) fail = !wwait(s_full, uint32_t(it & 1), 41);
-      uint32_t sr[64];
-      if (!fail) {
-        fence_after_sync();
-        tmem_ld32(trow + hf * 64, *reinterpret_cast<uint32_t(*)[32]>(sr));
-        tmem_ld32(trow + hf * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
-        tmem_ld_wait();
-        fence_before_sync();
-        mbar_arrive(s_empty);  // S in TMEM is free for the next item
-      } else {
-#pragma unroll
-        for (int i = 0; i < 64; ++i) sr[i] = 0u;
-      }
-      if constexpr (REL) {
-        // s = q.k + q.posKey[p] + k.posQuery[p], p = relidx[i][j] (local positions), over the kept keys
-        const float* c2p = p.rel_tables + (int64_t(row) * 2 * p.H + hg0 + hh) * p.NP;
-        const uint32_t* ridx = p.relidx + int64_t(row - sstart) * p.L - sstart;
+    uint8_t* prow = sP + g * 16384 + r_local * 128;
+    const int pairs = HG >> 1;  // full head pairs (their items alternate between the streams)
+    int u = 0;                  // stream-local item index
+    float l_prev = 0.f;
+    // Running state of the current head: m = the reference point of the exponentials (scaled
+    // log2 units), moved only when a key tile's maximum exceeds it by more than 8 (probabilities
+    // stay <= 2^8, exact in f16 up to the rounding; O in TMEM is rescaled then); l = the row sum.
+    bool started = false;
+    float m = 0.f, l = 0.f;
+    for (int hh = split ? 0 : g; hh < HG && ok; hh += 2) {
+      started = false;
+      m = 0.f;
+      l = 0.f;
+      const int base = (hh >> 1) * 2 * nkt;  // global index of the head pair's first item
+      const bool paired = (hh >> 1) < pairs;
+      for (int j = split ? g : 0; j < nkt; j += split ? 2 : 1, ++u) {
+        // global item index
+        const int it = split ? j : paired ? base + 2 * j + g : base + j;
+        const int k0 = kstart + j * TK;
+        const int clo = min(max(lo - k0, 0), 64), chi = min(max(hi - k0, 0), 64);
+        // keep masks of the two 32-key chunks: in the row's key range, present, unmasked
+        uint32_t km[2];
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
-          if (!__any_sync(0xffffffffu, km[c] != 0u)) continue;
+          const int a = min(max(clo - 32 * c, 0), 32), b = min(max(chi - 32 * c, 0), 32);
+          const uint32_t below_b = b >= 32 ? 0xffffffffu : ((1u << b) - 1u);
+          const uint32_t below_a = a >= 32 ? 0xffffffffu : ((1u << a) - 1u);
+          km[c] = (below_b & ~below_a) & vbits[j * 2 + c];
+        }
+        if (!wwait(&s_full[g], uint32_t(u & 1), 41)) { ok = false; break; }
+        uint32_t sr[64];
+        fence_after_sync();
+        tmem_ld32(s_addr, *reinterpret_cast<uint32_t(*)[32]>(sr));
+        tmem_ld32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
+        tmem_ld_wait();
+        fence_before_sync();
+        mbar_arrive(&s_empty[g]);  // S in TMEM is free for this stream's next item
+        if constexpr (REL) {
+          // s = q.k + q.posKey[p] + k.posQuery[p], p = relidx[i][j] (local positions), over the kept keys
+          const float* c2p = p.rel_tables + (int64_t(row) * 2 * p.H + hg0 + hh) * p.NP;
+          const uint32_t* ridx = p.relidx + int64_t(row - sstart) * p.L - sstart;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            if ((km[c] >> i) & 1u) {
-              const int j = k0 + c * 32 + i;
-              const uint32_t pp = __ldg(ridx + j);
-              const float* p2c = p.rel_tables + ((int64_t(j) * 2 + 1) * p.H + hg0 + hh) * p.NP;
-              sr[c * 32 + i] = __float_as_uint(__uint_as_float(sr[c * 32 + i]) + __ldg(c2p + pp) + __ldg(p2c + pp));
+          for (int c = 0; c < 2; ++c) {
+            if (!__any_sync(0xffffffffu, km[c] != 0u)) continue;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              if ((km[c] >> i) & 1u) {
+                const int kj = k0 + c * 32 + i;
+                const uint32_t pp = __ldg(ridx + kj);
+                const float* p2c = p.rel_tables + ((int64_t(kj) * 2 + 1) * p.H + hg0 + hh) * p.NP;
+                sr[c * 32 + i] = __float_as_uint(__uint_as_float(sr[c * 32 + i]) + __ldg(c2p + pp) + __ldg(p2c + pp));
+              }
             }
           }
         }
-      }
-      // the row maximum of the kept raw scores: this half, then both halves
-      float mr[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        // the row maximum of the kept raw scores
+        float mr[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        // warp-uniform cases: every lane keeps all 32 keys (no masks), none keeps any, or mixed
-        if (__all_sync(0xffffffffu, km[c] == 0xffffffffu)) {
+        for (int c = 0; c < 2; ++c) {
+          // warp-uniform cases: every lane keeps all 32 keys (no masks), none keeps any, or mixed
+          if (__all_sync(0xffffffffu, km[c] == 0xffffffffu)) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 2)
-            mr[(i >> 1) & 3] = fmax3(mr[(i >> 1) & 3], __uint_as_float(sr[32 * c + i]), __uint_as_float(sr[32 * c + i + 1]));
-        } else if (__any_sync(0xffffffffu, km[c] != 0u)) {
+            for (int i = 0; i < 32; i += 2)
+              mr[(i >> 1) & 3] = fmax3(mr[(i >> 1) & 3], __uint_as_float(sr[32 * c + i]), __uint_as_float(sr[32 * c + i + 1]));
+          } else if (__any_sync(0xffffffffu, km[c] != 0u)) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 2)
-            mr[(i >> 1) & 3] = fmax3(mr[(i >> 1) & 3],
-                                     ((km[c] >> i) & 1u) ? __uint_as_float(sr[32 * c + i]) : -INFINITY,
-                                     ((km[c] >> (i + 1)) & 1u) ? __uint_as_float(sr[32 * c + i + 1]) : -INFINITY);
+            for (int i = 0; i < 32; i += 2)
+              mr[(i >> 1) & 3] = fmax3(mr[(i >> 1) & 3],
+                                       ((km[c] >> i) & 1u) ? __uint_as_float(sr[32 * c + i]) : -INFINITY,
+                                       ((km[c] >> (i + 1)) & 1u) ? __uint_as_float(sr[32 * c + i + 1]) : -INFINITY);
+          }
         }
-      }
-      const float pm = fmaxf(fmaxf(mr[0], mr[1]), fmaxf(mr[2], mr[3]));
-      float* xm = xmax + ((it & 1) * 2) * 128;
-      float* xl = xsum + ((it & 1) * 2) * 128;
-      xm[hf * 128 + r_local] = pm;
-      if constexpr (!C::SUMS) xl[hf * 128 + r_local] = l_prev;  // the finished head's half sum
-      if (named_bar_any(pair_bar, 64, fail)) { ok = false; break; }
-      const float mraw = fmaxf(pm, xm[(hf ^ 1) * 128 + r_local]);
-      float lt_prev = 0.f;
-      if constexpr (!C::SUMS) lt_prev = l_prev + xl[(hf ^ 1) * 128 + r_local];
-      float corr = 1.f;
-      if (mraw > -INFINITY) {
-        const float cand = mraw * p.scale_log2;
-        if (!started) {
-          m = cand;
-          started = true;
-        } else if (cand > m + 8.f) {
-          corr = ex2_approx(m - cand);
-          m = cand;
+        const float mraw = fmaxf(fmaxf(mr[0], mr[1]), fmaxf(mr[2], mr[3]));
+        float corr = 1.f;
+        if (mraw > -INFINITY) {
+          const float cand = mraw * p.scale_log2;
+          if (!started) {
+            m = cand;
+            started = true;
+          } else if (cand > m + 8.f) {
+            corr = ex2_approx(m - cand);
+            m = cand;
+          }
         }
-      }
-      // P of the previous item is free once its PV product is done (it has long been, as a
-      // rule); this also keeps the observed PV phases at most one behind
-      if (it >= 1 && !wait_pv(it - 1)) {
-        ok = false;  // the pair ends together at the next item's barrier
-        *abort_flag = 1;
-        continue;
-      }
-      if (__any_sync(0xffffffffu, corr != 1.f)) {
-        // rescale this thread's columns of O (the PV products so far) before this item's PV
-        const uint32_t o_addr = trow + 128 + uint32_t((hh & 1) * D + hf * (D / 2));
+        // P of this stream's previous item is free, and O holds all its products, once its PV
+        // product is done (it has long been, as a rule)
+        if (u >= 1 && !wait_pv(u - 1)) { ok = false; break; }
+        if (!split && j == 0 && hh >= 2) finish_head(hh - 2, l_prev);  // before this head's first PV overwrites O
+        if (__any_sync(0xffffffffu, corr != 1.f)) {
+          // rescale O (the PV products so far) before this item's PV
 #pragma unroll 1
-        for (int c = 0; c < D / 2; c += 8) {
-          uint32_t r[8];
-          tmem_ld8(o_addr + c, r);
-          tmem_ld_wait();
+          for (int c = 0; c < D; c += 8) {
+            uint32_t r[8];
+            tmem_ld8(o_addr + c, r);
+            tmem_ld_wait();
 #pragma unroll
-          for (int e = 0; e < 8; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * corr);
-          tmem_st8(o_addr + c, r);
-        }
-        if constexpr (C::SUMS) {
-          if (hf == 0) {  // the row-sum columns, once per row
-            const uint32_t l_addr = trow + 192 + uint32_t((hh & 1) * 16);
+            for (int e = 0; e < 8; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * corr);
+            tmem_st8(o_addr + c, r);
+          }
+          if constexpr (C::SUMS) {
+            const uint32_t l_addr = trow + 192 + uint32_t(g * 16);
             uint32_t r[8];
             tmem_ld8(l_addr, r);
             tmem_ld_wait();
@@ -489,86 +497,129 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
             for (int e = 0; e < 8; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * corr);
             tmem_st8(l_addr, r);
           }
+          tmem_st_wait();
         }
-        tmem_st_wait();
-      }
-      // p = exp2(s scale log2e - m) in f16, into this row of P block hf (128-byte swizzled)
-      float ls[4] = {0.f, 0.f, 0.f, 0.f};
-      uint8_t* prow = sP + hf * 16384 + r_local * 128;
+        // p = exp2(s scale log2e - m) in f16, into this row of the stream's P block (128-byte swizzled)
+        float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const uint32_t k = km[c];
-        const bool all = __all_sync(0xffffffffu, k == 0xffffffffu);
-        const bool any = __any_sync(0xffffffffu, k != 0u);
+        for (int c = 0; c < 2; ++c) {
+          const uint32_t k = km[c];
+          const bool all = __all_sync(0xffffffffu, k == 0xffffffffu);
+          const bool any = __any_sync(0xffffffffu, k != 0u);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {  // keys 8 q .. 8 q + 7 of the chunk: one 16-byte chunk of P
-          uint32_t pk[4] = {0u, 0u, 0u, 0u};
-          if (all) {
+          for (int q = 0; q < 4; ++q) {  // keys 8 q .. 8 q + 7 of the chunk: one 16-byte chunk of P
+            uint32_t pk[4] = {0u, 0u, 0u, 0u};
+            if (all) {
 #pragma unroll
-            for (int e2 = 0; e2 < 4; ++e2) {
-              const int i = 8 * q + 2 * e2;
-              const float2 xx = ffma2(make_float2(__uint_as_float(sr[32 * c + i]), __uint_as_float(sr[32 * c + i + 1])),
-                                      make_float2(p.scale_log2, p.scale_log2), make_float2(-m, -m));
-              const float x0 = ex2_approx(xx.x);
-              const float x1 = ex2_approx(xx.y);
-              if constexpr (!C::SUMS) {
-                ls[i & 3] += x0;
-                ls[(i + 1) & 3] += x1;
+              for (int e2 = 0; e2 < 4; ++e2) {
+                const int i = 8 * q + 2 * e2;
+                const float2 xx = ffma2(make_float2(__uint_as_float(sr[32 * c + i]), __uint_as_float(sr[32 * c + i + 1])),
+                                        make_float2(p.scale_log2, p.scale_log2), make_float2(-m, -m));
+                const float x0 = ex2_approx(xx.x);
+                const float x1 = ex2_approx(xx.y);
+                if constexpr (!C::SUMS) {
+                  ls[i & 3] += x0;
+                  ls[(i + 1) & 3] += x1;
+                }
+                __half2 hv = __floats2half2_rn(x0, x1);
+                pk[e2] = *reinterpret_cast<uint32_t*>(&hv);
               }
-              __half2 hv = __floats2half2_rn(x0, x1);
-              pk[e2] = *reinterpret_cast<uint32_t*>(&hv);
-            }
-          } else if (any) {
+            } else if (any) {
 #pragma unroll
-            for (int e2 = 0; e2 < 4; ++e2) {
-              float pv[2];
-              const int i0 = 8 * q + 2 * e2;
-              const float2 xx = ffma2(make_float2(__uint_as_float(sr[32 * c + i0]), __uint_as_float(sr[32 * c + i0 + 1])),
-                                      make_float2(p.scale_log2, p.scale_log2), make_float2(-m, -m));
-              const float xs[2] = {xx.x, xx.y};
+              for (int e2 = 0; e2 < 4; ++e2) {
+                float pv[2];
+                const int i0 = 8 * q + 2 * e2;
+                const float2 xx = ffma2(make_float2(__uint_as_float(sr[32 * c + i0]), __uint_as_float(sr[32 * c + i0 + 1])),
+                                        make_float2(p.scale_log2, p.scale_log2), make_float2(-m, -m));
+                const float xs[2] = {xx.x, xx.y};
 #pragma unroll
-              for (int e = 0; e < 2; ++e) {
-                const int i = i0 + e;
-                const float x = ex2_approx(xs[e]);
-                pv[e] = ((k >> i) & 1u) ? x : 0.f;
-                if constexpr (!C::SUMS) ls[i & 3] += pv[e];
+                for (int e = 0; e < 2; ++e) {
+                  const int i = i0 + e;
+                  const float x = ex2_approx(xs[e]);
+                  pv[e] = ((k >> i) & 1u) ? x : 0.f;
+                  if constexpr (!C::SUMS) ls[i & 3] += pv[e];
+                }
+                __half2 hv = __floats2half2_rn(pv[0], pv[1]);
+                pk[e2] = *reinterpret_cast<uint32_t*>(&hv);
               }
-              __half2 hv = __floats2half2_rn(pv[0], pv[1]);
-              pk[e2] = *reinterpret_cast<uint32_t*>(&hv);
             }
+            const int ch = c * 4 + q;
+            *reinterpret_cast<uint4*>(prow + ((ch ^ (r_local & 7)) * 16)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
           }
-          const int ch = c * 4 + q;
-          *reinterpret_cast<uint4*>(prow + ((ch ^ (r_local & 7)) * 16)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
-      }
-      l = l * corr + ((ls[0] + ls[1]) + (ls[2] + ls[3]));  // (corr rescales the sum so far)
-      // value rows of masked or absent keys become zero before the PV product
-      const int vs = it % C::VS;
-      if (!wwait(&v_full[vs], uint32_t(it / C::VS) & 1, 42)) {
-        ok = false;
-        *abort_flag = 1;
-        continue;
-      }
-      if (!((vbits[j * 4 + (vrow >> 5)] >> (vrow & 31)) & 1u)) {
-        uint4* vr = reinterpret_cast<uint4*>(sV + vs * C::TILE + vrow * C::ROW_BYTES + vpart * (C::ROW_BYTES / 2));
+        l = l * corr + ((ls[0] + ls[1]) + (ls[2] + ls[3]));  // (corr rescales the sum so far)
+        // value rows of masked or absent keys become zero before the PV product
+        const int vs = it % C::VS;
+        if (!wwait(&v_full[vs], uint32_t(it / C::VS) & 1, 42)) { ok = false; break; }
+        if (!((vbits[j * 2 + (vrow >> 5)] >> (vrow & 31)) & 1u)) {
+          uint4* vr = reinterpret_cast<uint4*>(sV + vs * C::KTILE + vrow * C::ROW_BYTES + vpart * (C::ROW_BYTES / 2));
 #pragma unroll
-        for (int q = 0; q < C::ROW_BYTES / 32; ++q) vr[q] = make_uint4(0, 0, 0, 0);
+          for (int q = 0; q < C::ROW_BYTES / 32; ++q) vr[q] = make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async_smem();
+        fence_before_sync();
+        mbar_arrive(&p_full[g]);
       }
-      fence_proxy_async_smem();
-      fence_before_sync();
-      mbar_arrive(p_full);
-      if (pending) {  // the previous head's PV products are all done; its O is in the other buffer
-        finish_head(hh - 1, lt_prev);
-        pending = false;
+      l_prev = l;
+    }
+    // the stream's last head, once its last PV product is done
+    if (ok && u > 0) ok = wait_pv(u - 1);
+    if constexpr (!split) {
+      if (ok && u > 0) finish_head(g + 2 * ((HG - 1 - g) >> 1), l_prev);
+    } else {
+      // Combine the two streams' parts of the head: m = max(m0, m1), O = sum_g 2^(m_g - m) O_g,
+      // l = sum_g 2^(m_g - m) l_g (a stream without a kept key, or without items, adds nothing:
+      // select, not multiply, so its TMEM is never read into the sum). The thread of stream g
+      // writes the columns [g D / 2, (g + 1) D / 2) of the row.
+      float* xm = reinterpret_cast<float*>(smem + C::XCH_OFF);
+      float* xl = xm + 2 * 128;
+      xm[g * 128 + r_local] = (u > 0 && started) ? m : -INFINITY;
+      if constexpr (!C::SUMS) xl[g * 128 + r_local] = l;
+      if (named_bar_any(1 + quarter, 64, !ok)) {
+        ok = false;
+      } else {
+        const float m0 = xm[r_local], m1 = xm[128 + r_local];
+        const float mm = fmaxf(m0, m1);
+        const bool use0 = m0 > -INFINITY, use1 = m1 > -INFINITY;
+        const float f0 = use0 ? ex2_approx(m0 - mm) : 0.f, f1 = use1 ? ex2_approx(m1 - mm) : 0.f;
+        float l0, l1;
+        if constexpr (C::SUMS) {
+          uint32_t r0[8], r1[8];
+          tmem_ld8(trow + 192, r0);
+          tmem_ld8(trow + 192 + 16, r1);
+          tmem_ld_wait();
+          l0 = __uint_as_float(r0[0]);
+          l1 = __uint_as_float(r1[0]);
+        } else {
+          l0 = xl[r_local];
+          l1 = xl[128 + r_local];
+        }
+        const float lt = (use0 ? f0 * l0 : 0.f) + (use1 ? f1 * l1 : 0.f);
+        const bool live = qvalid && lt > 0.f;
+        const float inv = live ? 1.0f / lt : 0.f;
+        uint4* dst = reinterpret_cast<uint4*>(p.ctx + int64_t(row) * H * D + int64_t(hg0) * D + g * (D / 2));
+#pragma unroll
+        for (int c = 0; c < D / 2; c += 8) {
+          uint32_t a0[8], a1[8];
+          tmem_ld8(trow + 128 + uint32_t(g * (D / 2) + c), a0);
+          tmem_ld8(trow + 128 + uint32_t(D + g * (D / 2) + c), a1);
+          tmem_ld_wait();
+          __half2 hv[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float v[2];
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+              const float o0 = use0 ? f0 * __uint_as_float(a0[2 * e + t]) : 0.f;
+              const float o1 = use1 ? f1 * __uint_as_float(a1[2 * e + t]) : 0.f;
+              v[t] = live ? (o0 + o1) * inv : 0.f;
+            }
+            hv[e] = __floats2half2_rn(v[0], v[1]);
+          }
+          if (in_range) dst[c / 8] = *reinterpret_cast<uint4*>(hv);
+        }
       }
     }
-    if (ok && NI > 0) ok = wait_pv(NI - 1);
-    // the last head's half sums cross in the exchange slots of item NI (free: the partner read
-    // those of item NI - 2 before it passed the barrier of item NI - 1)
-    float* xl_end = xsum + ((NI & 1) * 2) * 128;
-    if constexpr (!C::SUMS) xl_end[hf * 128 + r_local] = l;
-    if (named_bar_any(pair_bar, 64, !ok)) ok = false;
-    else if (NI > 0) finish_head(HG - 1, C::SUMS ? 0.f : l + xl_end[(hf ^ 1) * 128 + r_local]);
     if (!ok) *abort_flag = 1;
   }
   fence_before_sync();
@@ -670,15 +721,16 @@ __global__ void __launch_bounds__(128) relpos_tables_kernel(const __grid_constan
 // the launch would otherwise leave most SMs idle (short B = 1 calls).
 int heads_per_cta(int H, int tiles) {
   static const int sms = device_sms();
-  for (int g = 4; g > 1; --g)
+  for (int g = 4; g > 1; g -= 2)  // an even count keeps both softmax streams busy
     if (H % g == 0 && int64_t(tiles) * (H / g) >= int64_t(sms)) return g;
-  return 1;
+  return 1;  // one head per CTA: the two streams split its key tiles
 }
 template <int D, bool REL = false>
 void launch_tc(const AttnArgs& a, const SeqTable& seq, int T, cudaStream_t st) {
   static bool configured = false;
   if (!configured) {
-    KH_CUDA(cudaFuncSetAttribute(attn_tc_kernel<D, REL>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::SMEM));
+    KH_CUDA(cudaFuncSetAttribute(attn_tc_kernel<D, REL, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::SMEM));
+    KH_CUDA(cudaFuncSetAttribute(attn_tc_kernel<D, REL, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::SMEM));
     if (REL)
       KH_CUDA(cudaFuncSetAttribute(relpos_tables_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 49152 + 1024 + 64));
     configured = true;
@@ -698,7 +750,8 @@ void launch_tc(const AttnArgs& a, const SeqTable& seq, int T, cudaStream_t st) {
     relpos_tables_kernel<<<g, 128, 49152 + 1024 + 64, st>>>(tq, tk, tp, rp);
   }
   const uint64_t cols = uint64_t(3) * a.H * D;
-  const CUtensorMap& tm = tensor_map_f16(a.qkv, uint64_t(T), cols, cols, D, 128, D * 2);
+  const CUtensorMap& tmq = tensor_map_f16(a.qkv, uint64_t(T), cols, cols, D, TQ, D * 2);
+  const CUtensorMap& tmkv = tensor_map_f16(a.qkv, uint64_t(T), cols, cols, D, TK, D * 2);
   Params p;
   p.mask = a.mask;
   p.seq_start = seq.start;
@@ -716,7 +769,8 @@ void launch_tc(const AttnArgs& a, const SeqTable& seq, int T, cudaStream_t st) {
   p.L = a.L;
   p.NP = a.np;
   dim3 grid(seq.nptiles, a.H / p.HG);
-  attn_tc_kernel<D, REL><<<grid, THREADS, Cfg<D>::SMEM, st>>>(tm, p);
+  if (p.HG == 1) attn_tc_kernel<D, REL, true><<<grid, THREADS, Cfg<D>::SMEM, st>>>(tmq, tmkv, p);
+  else attn_tc_kernel<D, REL, false><<<grid, THREADS, Cfg<D>::SMEM, st>>>(tmq, tmkv, p);
 }
 
 // ---- packed attention whose sequence table lives in static device memory ----
@@ -801,8 +855,10 @@ int32_t* noalloc_scratch() {
     const cudaError_t e = cudaGetSymbolAddress(&ptr, kh_attn_noalloc_scratch);
     if (e != cudaSuccess)
       throw CudaError(std::string("kh_attention_f16_noalloc: cudaGetSymbolAddress: ") + cudaGetErrorString(e));
-    KH_CUDA(cudaFuncSetAttribute(attn_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<32>::SMEM));
-    KH_CUDA(cudaFuncSetAttribute(attn_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<64>::SMEM));
+    KH_CUDA(cudaFuncSetAttribute(attn_tc_kernel<32, false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<32>::SMEM));
+    KH_CUDA(cudaFuncSetAttribute(attn_tc_kernel<64, false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<64>::SMEM));
+    KH_CUDA(cudaFuncSetAttribute(attn_tc_kernel<32, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<32>::SMEM));
+    KH_CUDA(cudaFuncSetAttribute(attn_tc_kernel<64, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<64>::SMEM));
     per_device[dev] = static_cast<int32_t*>(ptr);
   }
   return per_device[dev];
@@ -821,7 +877,7 @@ void attention_f16_noalloc(const void* qkv, const float* mask, void* ctx, const 
   if (window < 0) throw ArgError("kh_attention_f16_noalloc: window must be >= 0");
   if ((reinterpret_cast<uintptr_t>(qkv) & 15) || (reinterpret_cast<uintptr_t>(ctx) & 15))
     throw ArgError("kh_attention_f16_noalloc: qkv and ctx must be 16-byte aligned");
-  const int max_len = (MAXKT * TKEYS - TQ) / 2;
+  const int max_len = (MAXKT * TK - TQ) / 2;
   int64_t T = 0;
   for (int i = 0; i < n_seqs; ++i) {
     if (seq_lens[i] < 1 || seq_lens[i] > max_len)
@@ -836,9 +892,10 @@ void attention_f16_noalloc(const void* qkv, const float* mask, void* ctx, const 
   KH_CUDA(cudaMemcpyAsync(w + NA_LENS, seq_lens, size_t(n_seqs) * 4, cudaMemcpyHostToDevice, st));
   noalloc_starts_kernel<<<1, 1024, 0, st>>>(w, n_seqs);
   noalloc_rows_kernel<<<int((T + 255) / 256), 256, 0, st>>>(w, n_seqs, int(T));
-  CUtensorMap tm;
+  CUtensorMap tmq, tmkv;
   const uint64_t cols = uint64_t(3) * H * D;
-  encode_tensor_map_f16(&tm, qkv, uint64_t(T), cols, cols, D, 128, D * 2);
+  encode_tensor_map_f16(&tmq, qkv, uint64_t(T), cols, cols, D, TQ, D * 2);
+  encode_tensor_map_f16(&tmkv, qkv, uint64_t(T), cols, cols, D, TK, D * 2);
   Params p;
   p.mask = mask;
   p.seq_start = w + NA_START;
@@ -852,8 +909,11 @@ void attention_f16_noalloc(const void* qkv, const float* mask, void* ctx, const 
   p.window = window;
   p.scale_log2 = scale * 1.4426950408889634f;
   const dim3 grid(unsigned((T + TQ - 1) / TQ), unsigned(H / p.HG));
-  if (D == 64) attn_tc_kernel<64><<<grid, THREADS, Cfg<64>::SMEM, st>>>(tm, p);
-  else attn_tc_kernel<32><<<grid, THREADS, Cfg<32>::SMEM, st>>>(tm, p);
+  const bool one = p.HG == 1;
+  if (D == 64 && one) attn_tc_kernel<64, false, true><<<grid, THREADS, Cfg<64>::SMEM, st>>>(tmq, tmkv, p);
+  else if (D == 64) attn_tc_kernel<64, false, false><<<grid, THREADS, Cfg<64>::SMEM, st>>>(tmq, tmkv, p);
+  else if (one) attn_tc_kernel<32, false, true><<<grid, THREADS, Cfg<32>::SMEM, st>>>(tmq, tmkv, p);
+  else attn_tc_kernel<32, false, false><<<grid, THREADS, Cfg<32>::SMEM, st>>>(tmq, tmkv, p);
   KH_CUDA(cudaGetLastError());
 }
 
@@ -862,7 +922,7 @@ int attention_tile_q(bool) { return 64; }
 bool attention_tc_supported(bool f16, const AttnArgs& a) {
   // the key rows of one packed tile must fit the CTA's key-tile masks; relative attention on the
   // tensor cores takes 64-wide heads (DeBERTa-v2/v3) and needs its tables (AttnArgs::rel_tables)
-  if (!f16 || a.L > (MAXKT * TKEYS - TQ) / 2) return false;
+  if (!f16 || a.L > (MAXKT * TK - TQ) / 2) return false;
   if (a.rel) return a.D == 64 && a.np > 0;
   return a.D == 64 || a.D == 32;
 }
