@@ -717,11 +717,12 @@ __global__ void __launch_bounds__(128) relpos_tables_kernel(const __grid_constan
   }
 }
 
-// Heads per CTA: up to 4 (the CTA loads the keys of a tile once for all its heads), fewer when
-// the launch would otherwise leave most SMs idle (short B = 1 calls).
+// Heads per CTA: as many as keep every SM busy, up to 12 (the CTA computes the key masks of a
+// tile once for all its heads, and fewer, longer CTAs measured faster), an even number so both
+// softmax streams work; one head per CTA (split mode) for small launches.
 int heads_per_cta(int H, int tiles) {
   static const int sms = device_sms();
-  for (int g = 4; g > 1; g -= 2)  // an even count keeps both softmax streams busy
+  for (int g = 12; g > 1; g -= 2)  // an even count keeps both softmax streams busy
     if (H % g == 0 && int64_t(tiles) * (H / g) >= int64_t(sms)) return g;
   return 1;  // one head per CTA: the two streams split its key tiles
 }
