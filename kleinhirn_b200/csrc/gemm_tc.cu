@@ -122,18 +122,6 @@ __device__ __forceinline__ void stage32_sw128(uint8_t* tile, int r, int ch, cons
   }
 }
 
-// Row r of a staged tile with 64-byte rows (64-byte swizzle, a 32-column f16 box).
-__device__ __forceinline__ void stage32_sw64(uint8_t* tile, int r, const float (&v)[32]) {
-  uint8_t* row = tile + r * 64;
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    __half2 h[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) h[e] = __floats2half2_rn(v[q * 8 + 2 * e], v[q * 8 + 2 * e + 1]);
-    *reinterpret_cast<uint4*>(row + ((q ^ ((r >> 1) & 3)) * 16)) = *reinterpret_cast<uint4*>(h);
-  }
-}
-
 // Bias and activation of 32 accumulator columns [n, n + 32) of one row, in place.
 template <int MODE>
 __device__ __forceinline__ void bias_act32(float (&v)[32], const __half* bias, int n) {
