@@ -69,7 +69,8 @@ struct Cfg {
   // stream next to O); D = 64 has no TMEM room left and sums in the softmax threads.
   static constexpr bool SUMS = D == 32;
   static constexpr int XCH_OFF = BITS_OFF + MAXKT * 2 * 4;  // split mode: m and l of both streams, f32 [2][2][128]
-  static constexpr int ONES_OFF = XCH_OFF + 2 * 2 * 128 * 4;
+  static constexpr int LUT_OFF = XCH_OFF + 2 * 2 * 128 * 4;  // key masks of 4 bits as 4 words, [16]
+  static constexpr int ONES_OFF = LUT_OFF + 16 * 16;
   static constexpr int BAR_OFF = ONES_OFF + (SUMS ? 2048 : 0);  // ones: 16 rows x 64 keys
   static constexpr int USED = BAR_OFF + 512;
   // at least 100 KB so that no more than two CTAs (2 x 256 TMEM columns) share an SM
@@ -111,6 +112,8 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
   uint8_t* sV = smem + C::V_OFF;
   uint8_t* sP = smem + C::P_OFF;
   uint32_t* vbits = reinterpret_cast<uint32_t*>(smem + C::BITS_OFF);  // [tile][2]: key present, unmasked
+  // lut4[n]: the 4 keys of a nibble n of a keep mask as 32-bit masks (key kept: all ones)
+  uint4* lut4 = reinterpret_cast<uint4*>(smem + C::LUT_OFF);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* q_full = bars;             // [stream]
   uint64_t* q_empty = bars + 2;        // [stream]
@@ -182,6 +185,10 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
     fence_barrier_init();
     prefetch_tmap(&tmq);
     prefetch_tmap(&tmkv);
+  }
+  if (threadIdx.x < 16) {
+    const uint32_t n = threadIdx.x;
+    lut4[n] = make_uint4((n & 1u) ? ~0u : 0u, (n & 2u) ? ~0u : 0u, (n & 4u) ? ~0u : 0u, (n & 8u) ? ~0u : 0u);
   }
   if constexpr (C::SUMS) {
     // B operand of the row-sum MMA: 16 x 64 f16 ones (every swizzle of it is the same)
@@ -444,21 +451,33 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
             }
           }
         }
+        // warp-uniform cases per 32-key chunk: every lane keeps all keys, none keeps any, or mixed;
+        // in a mixed chunk a dropped key's score becomes -inf ((s & mask) | (~mask & bits(-inf)),
+        // whatever it was), so the maximum and the exponentials below need no masks
+        bool any_c[2];
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          any_c[c] = __any_sync(0xffffffffu, km[c] != 0u);
+          if (any_c[c] && !__all_sync(0xffffffffu, km[c] == 0xffffffffu)) {
+#pragma unroll
+            for (int i4 = 0; i4 < 8; ++i4) {
+              const uint4 mk = lut4[(km[c] >> (4 * i4)) & 0xFu];
+              const int i = 32 * c + 4 * i4;
+              sr[i] = (sr[i] & mk.x) | (~mk.x & 0xFF800000u);
+              sr[i + 1] = (sr[i + 1] & mk.y) | (~mk.y & 0xFF800000u);
+              sr[i + 2] = (sr[i + 2] & mk.z) | (~mk.z & 0xFF800000u);
+              sr[i + 3] = (sr[i + 3] & mk.w) | (~mk.w & 0xFF800000u);
+            }
+          }
+        }
         // the row maximum of the kept raw scores
         float mr[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
-          // warp-uniform cases: every lane keeps all 32 keys (no masks), none keeps any, or mixed
-          if (__all_sync(0xffffffffu, km[c] == 0xffffffffu)) {
+          if (any_c[c]) {
 #pragma unroll
             for (int i = 0; i < 32; i += 2)
               mr[(i >> 1) & 3] = fmax3(mr[(i >> 1) & 3], __uint_as_float(sr[32 * c + i]), __uint_as_float(sr[32 * c + i + 1]));
-          } else if (__any_sync(0xffffffffu, km[c] != 0u)) {
-#pragma unroll
-            for (int i = 0; i < 32; i += 2)
-              mr[(i >> 1) & 3] = fmax3(mr[(i >> 1) & 3],
-                                       ((km[c] >> i) & 1u) ? __uint_as_float(sr[32 * c + i]) : -INFINITY,
-                                       ((km[c] >> (i + 1)) & 1u) ? __uint_as_float(sr[32 * c + i + 1]) : -INFINITY);
           }
         }
         const float mraw = fmaxf(fmaxf(mr[0], mr[1]), fmaxf(mr[2], mr[3]));
@@ -503,13 +522,11 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
         float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
-          const uint32_t k = km[c];
-          const bool all = __all_sync(0xffffffffu, k == 0xffffffffu);
-          const bool any = __any_sync(0xffffffffu, k != 0u);
+          const bool any = any_c[c];
 #pragma unroll
           for (int q = 0; q < 4; ++q) {  // keys 8 q .. 8 q + 7 of the chunk: one 16-byte chunk of P
             uint32_t pk[4] = {0u, 0u, 0u, 0u};
-            if (all) {
+            if (any) {  // (a dropped key's score is -inf: its exponential is 0)
 #pragma unroll
               for (int e2 = 0; e2 < 4; ++e2) {
                 const int i = 8 * q + 2 * e2;
@@ -522,24 +539,6 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
                   ls[(i + 1) & 3] += x1;
                 }
                 __half2 hv = __floats2half2_rn(x0, x1);
-                pk[e2] = *reinterpret_cast<uint32_t*>(&hv);
-              }
-            } else if (any) {
-#pragma unroll
-              for (int e2 = 0; e2 < 4; ++e2) {
-                float pv[2];
-                const int i0 = 8 * q + 2 * e2;
-                const float2 xx = ffma2(make_float2(__uint_as_float(sr[32 * c + i0]), __uint_as_float(sr[32 * c + i0 + 1])),
-                                        make_float2(p.scale_log2, p.scale_log2), make_float2(-m, -m));
-                const float xs[2] = {xx.x, xx.y};
-#pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                  const int i = i0 + e;
-                  const float x = ex2_approx(xs[e]);
-                  pv[e] = ((k >> i) & 1u) ? x : 0.f;
-                  if constexpr (!C::SUMS) ls[i & 3] += pv[e];
-                }
-                __half2 hv = __floats2half2_rn(pv[0], pv[1]);
                 pk[e2] = *reinterpret_cast<uint32_t*>(&hv);
               }
             }
