@@ -3,7 +3,7 @@ models of every family, computed by the reference's own f64 executable specifica
 ``convert/k28_forward.py`` (``encoder`` + ``head_forward``, convert/k28_forward.py:148-264)
 imported from the reference checkout. Run in the build container, where the reference exists:
 
-    python tests/golden/make_golden.py [path to the reference checkout]
+    python tests/golden/make_golden.py <path to the reference checkout>
 
 The weights are not stored: they are regenerated from the recorded seed by
 kleinhirn_b200.synthetic.random_weights, and the file records the sha256 of the generated
@@ -151,4 +151,6 @@ def main(ref: Path) -> None:
 
 
 if __name__ == "__main__":
-    main(Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference"))
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <path to the reference checkout>")
+    main(Path(sys.argv[1]))

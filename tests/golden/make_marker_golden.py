@@ -13,7 +13,7 @@ Both specs fix their constants: LayerNorm eps 1e-7 (GLiNER2) and 1e-5 (Julia), R
 dimension of 64 (Julia), so the tiny models keep those. Run in the build container, where the
 reference exists:
 
-    python tests/golden/make_marker_golden.py [path to the reference checkout]
+    python tests/golden/make_marker_golden.py <path to the reference checkout>
 
 The weights are regenerated from the recorded seeds by kleinhirn_b200.synthetic.random_weights;
 the file records their sha256 so a change of the generator fails the tests. The tests read the
@@ -110,4 +110,6 @@ def main(ref: Path) -> None:
 
 
 if __name__ == "__main__":
-    main(Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference"))
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_marker_golden.py <path to the reference checkout>")
+    main(Path(sys.argv[1]))

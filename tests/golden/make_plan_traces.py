@@ -7,7 +7,7 @@ copies, every pipeline with its override constants, every bind group and dispatc
 output copy; buffers carry their sizes and the sha256 of their build-time contents (relidx,
 cossin, zero). Run in the build container, where the reference exists:
 
-    python tests/golden/make_plan_traces.py [path to the reference checkout]
+    python tests/golden/make_plan_traces.py <path to the reference checkout>
 
 The tests read the fixture only; they never open the reference.
 """
@@ -22,7 +22,9 @@ OUT = Path(__file__).resolve().parent / "plan_traces.json.gz"
 
 
 def main() -> None:
-    ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_plan_traces.py <path to the reference checkout>")
+    ref = Path(sys.argv[1])
     frozen = json.loads(gzip.decompress((ref / "tests/golden/k28/dispatch-traces.json.gz").read_bytes()))
     keep = {k: {"buffers": v["buffers"], "events": v["events"]}
             for k, v in frozen["traces"].items() if k.endswith("-normal") or k.endswith("-normal100")}

@@ -158,3 +158,71 @@ def test_relative_attention_f16(L, lens, span):
     err = np.abs(got[keep] - want[keep])
     tol = 4e-3 + 1e-2 * np.abs(want[keep])
     assert np.all(err <= tol), f"worst {err.max()} at {int(np.argmax(err - tol))}"
+
+
+def standard_ref(qkv16, mask, L, B, H, D, scale, window):
+    """attention_ref vectorised per (sequence, head), float64 (tests/wasm_plan.test.ts:299-333)."""
+    x = qkv16.astype(np.float64).reshape(B, L, 3, H, D)
+    m = mask.reshape(B, L) > 0.5
+    pos = np.arange(L)
+    near = np.abs(pos[:, None] - pos[None, :]) <= window if window else np.ones((L, L), dtype=bool)
+    out = np.zeros((B, L, H, D))
+    for b in range(B):
+        keep = m[b][None, :] & near
+        for h in range(H):
+            q = np.nan_to_num(x[b, :, 0, h])
+            k = np.nan_to_num(x[b, :, 1, h])
+            v = np.nan_to_num(x[b, :, 2, h]) * m[b][:, None]
+            s = np.where(keep, (q @ k.T) * scale, -np.inf)
+            with np.errstate(invalid="ignore"):  # rows without a kept key: replaced by zeros below
+                e = np.exp(s - s.max(axis=1, keepdims=True))
+                o = (e / e.sum(axis=1, keepdims=True)) @ v
+            out[b, :, h] = np.where(m[b][:, None], o, 0.0)
+    return out.reshape(-1)
+
+
+# Large launches spread 2, 4, 6 or 12 heads over the two softmax streams of a CTA (the C5 bulk
+# path runs 12): B sequences of a 128-row bucket give B packed tiles, and the head group is the
+# largest even divisor of 12 that still fills the 148 SMs.
+@pytest.mark.parametrize("D", [32, 64])
+@pytest.mark.parametrize("B,window", [(30, 0), (60, 0), (100, 16), (160, 0)], ids=["hg2", "hg4", "hg6-window", "hg12"])
+def test_packed_attention_head_groups(D, B, window):
+    L, H = 128, 12
+    hd = H * D
+    rng = np.random.default_rng(B + D)
+    lens = rng.integers(40, L + 1, B).tolist()
+    qkv = (rng.standard_normal(B * L * 3 * hd) * 1.5).astype(np.float16)
+    mask = prefix_mask(L, lens)
+    qkv.reshape(B * L, 3 * hd)[mask <= 0.5] = np.nan
+    scale = D ** -0.5
+    want = standard_ref(qkv, mask, L, B, H, D, scale, window)
+    got = run_attention(qkv, mask, L, B, H, D, scale, window, B * L)
+    keep = np.repeat(mask > 0, hd)
+    assert np.all(got[~keep] == 0), "masked query rows must be exactly zero"
+    err = np.abs(got[keep] - want[keep])
+    tol = 4e-3 + 1e-2 * np.abs(want[keep])
+    assert np.all(err <= tol), f"worst {err.max()} at {int(np.argmax(err - tol))}"
+
+
+def test_relative_attention_head_groups():
+    """DeBERTa's relative attention on a launch large enough for 4 heads per CTA (both streams)."""
+    B, L, H, D, span = 160, 128, 4, 64, 64
+    hd = H * D
+    rng = np.random.default_rng(77)
+    lens = rng.integers(30, L + 1, B).tolist()
+    qkv = (rng.standard_normal(B * L * 3 * hd) * 1.2).astype(np.float16)
+    mask = prefix_mask(L, lens)
+    qkv.reshape(B * L, 3 * hd)[mask <= 0.5] = np.nan
+    idx = np.zeros(L * L, dtype=np.uint32)
+    for i in range(L):
+        idx[i * L:(i + 1) * L] = np.clip(i - np.arange(L) + span, 0, 2 * span - 1)
+    pk = (rng.standard_normal((2 * span, hd)) * 0.8).astype(np.float16)
+    pq = (rng.standard_normal((2 * span, hd)) * 0.8).astype(np.float16)
+    scale_div = math.sqrt(3 * D)
+    want = relative_ref(qkv, mask, L, B, H, D, scale_div, idx, pk, pq)
+    got, _ = run_relative(qkv, mask, L, B, H, D, scale_div, idx, pk, pq, B * L)
+    keep = np.repeat(mask > 0, hd)
+    assert np.all(got[~keep] == 0), "masked query rows must be exactly zero"
+    err = np.abs(got[keep] - want[keep])
+    tol = 4e-3 + 1e-2 * np.abs(want[keep])
+    assert np.all(err <= tol), f"worst {err.max()} at {int(np.argmax(err - tol))}"
