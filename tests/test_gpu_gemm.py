@@ -174,3 +174,30 @@ def test_addnorm_epilogue(N, K, M):
     var = ((v - mean) ** 2).mean(axis=1, keepdims=True)
     want = f16((v - mean) / np.sqrt(var + eps) * g.astype(np.float64) + beta.astype(np.float64))
     assert_f16_close(got, want.reshape(-1), f"add+layernorm N={N} K={K}")
+
+
+# Launches of the C5 size: many 256-row blocks per CTA pair (the last one half full), the
+# persistent tile loop, both accumulators and the stage ring wrapping many times.
+@pytest.mark.parametrize("N,K,act", [(1152, 384, 0), (1536, 384, 2), (768, 200, 3)])
+def test_gemm_row_block_schedule(N, K, act):
+    from kleinhirn_b200.backend import CudaBackend
+    M = 80_000  # 313 row blocks (the last one half full) against 74 pairs
+    rng = np.random.default_rng(N + K)
+    A = (rng.standard_normal((M, K)) * 0.5).astype(np.float16)
+    W = (rng.standard_normal((N, K)) * 0.05).astype(np.float16)
+    b = (rng.standard_normal(N) * 0.1).astype(np.float16)
+    plan = f16plan([{"name": "mm", "kernel": "mmtile", "constants": {"M": M, "N": N, "K": K, "ACT": act},
+                     "bind": ["a", "w:w", "w:b", "c"], "dispatch": [1, "rows32"]}],
+                   {"a": (M * K, None), "c": (M * N, None)}, M, "c")
+    be = CudaBackend()
+    be.add_tensor("w", W)
+    be.add_tensor("b", b)
+    r = be.runner(plan)
+    r.write_buffer("a", A)
+    r.run(M)
+    C = r.read_buffer("c", 2 * M * N).view(np.float16).reshape(M, N)
+    r.destroy()
+    be.dispose()
+    rows = np.unique(np.concatenate([rng.integers(0, M, 3000), np.arange(M - 300, M), np.arange(0, 300)]))
+    want = f16(ACT64[act](A[rows].astype(np.float64) @ W.astype(np.float64).T + b.astype(np.float64)))
+    assert_f16_close(C[rows].astype(np.float64).reshape(-1), want.reshape(-1), f"gemm {M}x{N}x{K} act {act}")
