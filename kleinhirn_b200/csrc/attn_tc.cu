@@ -547,13 +547,17 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
           }
         }
         l = l * corr + ((ls[0] + ls[1]) + (ls[2] + ls[3]));  // (corr rescales the sum so far)
-        // value rows of masked or absent keys become zero before the PV product
-        const int vs = it % C::VS;
-        if (!wwait(&v_full[vs], uint32_t(it / C::VS) & 1, 42)) { ok = false; break; }
-        if (!((vbits[j * 2 + (vrow >> 5)] >> (vrow & 31)) & 1u)) {
-          uint4* vr = reinterpret_cast<uint4*>(sV + vs * C::KTILE + vrow * C::ROW_BYTES + vpart * (C::ROW_BYTES / 2));
+        // value rows of masked or absent keys become zero before the PV product (a tile whose 64
+        // key rows are all present and unmasked, the rule in packed bulk runs, needs nothing:
+        // the MMA thread itself waits for V)
+        if ((vbits[j * 2] & vbits[j * 2 + 1]) != 0xffffffffu) {
+          const int vs = it % C::VS;
+          if (!wwait(&v_full[vs], uint32_t(it / C::VS) & 1, 42)) { ok = false; break; }
+          if (!((vbits[j * 2 + (vrow >> 5)] >> (vrow & 31)) & 1u)) {
+            uint4* vr = reinterpret_cast<uint4*>(sV + vs * C::KTILE + vrow * C::ROW_BYTES + vpart * (C::ROW_BYTES / 2));
 #pragma unroll
-          for (int q = 0; q < C::ROW_BYTES / 32; ++q) vr[q] = make_uint4(0, 0, 0, 0);
+            for (int q = 0; q < C::ROW_BYTES / 32; ++q) vr[q] = make_uint4(0, 0, 0, 0);
+          }
         }
         fence_proxy_async_smem();
         fence_before_sync();
