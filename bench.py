@@ -38,9 +38,11 @@ BUCKET = 512
 
 
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one GEMM launch on a 262,144-row
-# chunk, mean of the four GEMM launches of a layer (qkv 0.750 GB, FFN-in 0.953 GB, attnOut +
-# LayerNorm 0.568 GB, FFN-out + LayerNorm 1.194 GB), from one ncu capture each.
+# chunk, mean of the four GEMM launches of a layer (qkv 0.753 GB, FFN-in 0.951 GB, attnOut +
+# LayerNorm 0.568 GB, FFN-out + LayerNorm 1.195 GB), from one ncu capture each; every term is
+# rows x a per-row byte count, so a launch over another chunk size scales with its rows.
 GEMM_TRAFFIC_BYTES = 866.2e6
+GEMM_TRAFFIC_ROWS = 262144
 GEMM_TRAFFIC_SOURCE = "ncu, profiles/gemm_pair_c5.md and profiles/gemm_addln_c5.md"
 
 
@@ -51,7 +53,8 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--pairs", type=int, default=65536)
-    ap.add_argument("--chunk-tokens", type=int, default=262144)
+    ap.add_argument("--chunk-tokens", type=int, default=0,
+                    help="packed rows per bulk chunk (0: even chunks of at most 524,288 rows)")
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -129,7 +132,7 @@ def run_config(args):
             emb, types, lens = packed_inputs(spec, table, ids)
             plan = build_plan(spec, head, 512, 1, 0, f16)
             r = be.runner(plan)
-            bulk = be.bulk(r, int(lens.sum()), len(lens), args.chunk_tokens)
+            bulk = be.bulk(r, int(lens.sum()), len(lens), chunk_size(int(lens.sum()), args.chunk_tokens))
             tt = types if "typeIds" in plan["inputs"] else None
             for _ in range(max(3, args.warmup)):
                 bulk.run_batch(lens, emb, tt)
@@ -255,6 +258,16 @@ def shard_pairs(lens: np.ndarray, world: int, rank: int) -> np.ndarray:
     return mine[np.argsort(lens[mine], kind="stable")]
 
 
+def chunk_size(tokens: int, requested: int) -> int:
+    """Packed rows per bulk chunk: as asked, or the rank's rows in even chunks of at most
+    524,288 (long launches keep the tail waves of the GEMMs small; even chunks avoid a short last
+    one), plus room for the sequence that does not fit exactly."""
+    if requested > 0:
+        return requested
+    n = max(1, -(-tokens // 524288))
+    return max(BUCKET, -(-tokens // n) + BUCKET)
+
+
 def make_workload(args):
     from kleinhirn_b200 import synthetic
     spec, head = synthetic.model(WORKLOAD)
@@ -360,7 +373,9 @@ def main():
     be = CudaBackend(w16, device=local)
     plan = build_plan(spec, head, BUCKET, 1, 0, True)
     runner = be.runner(plan)
-    bulk = be.bulk(runner, tokens, len(my_lens), args.chunk_tokens)
+    chunk_rows = chunk_size(tokens, args.chunk_tokens)
+    launch_rows = tokens / max(1, -(-tokens // chunk_rows))  # mean packed rows of one GEMM launch
+    bulk = be.bulk(runner, tokens, len(my_lens), chunk_rows)
     stream = torch.cuda.ExternalStream(be.stream, device=torch.device("cuda", local))
 
     # pinned host buffers of the e2e path: packed token ids (the word table lives on the device)
@@ -475,7 +490,8 @@ def main():
             "roofline": {"bound": "tensor", "kernel": "gemm", "achieved": achieved, "peak": peaks["tflops"],
                          "unit": "TFLOP/s", "frac": achieved / peaks["tflops"] if peaks["tflops"] else None,
                          "peak_source": peaks["source"] + " bf16_tflops_sustained",
-                         "traffic": GEMM_TRAFFIC_BYTES, "traffic_unit": "bytes per launch",
+                         "traffic": GEMM_TRAFFIC_BYTES * launch_rows / GEMM_TRAFFIC_ROWS,
+                         "traffic_unit": "bytes per launch (mean over the GEMM launches)",
                          "traffic_source": GEMM_TRAFFIC_SOURCE,
                          "share_of_forward": gemm_ms / total_prof if total_prof else None},
             "clocks": clocks.summary(),
