@@ -73,3 +73,26 @@ def test_shard_single_rank_identity():
     lens = np.array([5, 3, 9, 1], dtype=np.int64)
     mine = bench.shard_pairs(lens, 1, 0)
     assert sorted(mine.tolist()) == [0, 1, 2, 3]
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_chunks_are_even_and_bounded(world):
+    """Each rank's rows go in even bulk chunks of at most 524,288 (+ one bucket of room for the
+    sequence that does not fit exactly): the full C5 step on 1 GPU, and its shares on 2, 4, 8."""
+    from kleinhirn_b200 import synthetic
+    lens = synthetic.seq_lengths(bench.WORKLOAD, 65536, 1234)
+    for rank in range(world):
+        mine = bench.shard_pairs(lens, world, rank)
+        rows = int(lens[mine].sum())
+        chunk = bench.chunk_size(rows, 0)
+        n = -(-rows // chunk)
+        assert chunk <= 524288 + bench.BUCKET
+        # greedy packing of whole sequences fills the chunks: no short extra one
+        filled, count = 0, 1
+        for ln in lens[mine]:
+            if filled + ln > chunk:
+                count, filled = count + 1, 0
+            filled += int(ln)
+        assert count == n, (rows, chunk, count, n)
+    assert bench.chunk_size(3960, 0) >= 3960
+    assert bench.chunk_size(10, 777) == 777
