@@ -33,6 +33,7 @@
 // Two CTAs share an SM (256 TMEM columns and <= 108 KB of shared memory each).
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -731,14 +732,13 @@ int heads_per_cta(int H, int tiles) {
 }
 template <int D, bool REL = false>
 void launch_tc(const AttnArgs& a, const SeqTable& seq, int T, cudaStream_t st) {
-  static bool configured = false;
-  if (!configured) {
+  static std::atomic<uint64_t> configured{0};
+  once_per_device(configured, [] {
     KH_CUDA(cudaFuncSetAttribute(attn_tc_kernel<D, REL, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::SMEM));
     KH_CUDA(cudaFuncSetAttribute(attn_tc_kernel<D, REL, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<D>::SMEM));
     if (REL)
       KH_CUDA(cudaFuncSetAttribute(relpos_tables_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 49152 + 1024 + 64));
-    configured = true;
-  }
+  });
   if constexpr (REL) {
     // c2p / p2c tables of every packed row and head first
     const uint64_t cols = uint64_t(3) * a.H * D, hd = uint64_t(a.H) * D;

@@ -33,6 +33,7 @@
 
 #include <algorithm>
 #include <map>
+#include <atomic>
 #include <mutex>
 #include <tuple>
 
@@ -861,8 +862,9 @@ DevTensor gemm_geglu_bias(Ctx* ctx, const std::string& name, int N) {
 template <int BN, int MODE>
 static void launch_pair_mode(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const Params& p,
                              int tiles, cudaStream_t st) {
-  static int max_pairs = 0;
-  if (max_pairs == 0) {
+  static std::atomic<int> max_pairs_seen{0};
+  static std::atomic<uint64_t> configured{0};
+  once_per_device(configured, [] {
     KH_CUDA(cudaFuncSetAttribute(gemm_pair_kernel<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  PCfg<BN>::SMEM));
     cudaLaunchConfig_t cfg = {};
@@ -879,9 +881,9 @@ static void launch_pair_mode(const CUtensorMap& ma, const CUtensorMap& mb, const
     int n = 0;
     KH_CUDA(cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<BN, MODE>, &cfg));
     if (n <= 0) throw CudaError("gemm: no CTA pair fits on the device");
-    max_pairs = n;
-  }
-  const int pairs = std::min(tiles, max_pairs);
+    max_pairs_seen.store(n);  // the same on every B200
+  });
+  const int pairs = std::min(tiles, max_pairs_seen.load());
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -964,13 +966,14 @@ template <int NF>
 static void launch_addln_nf(const void* A, const void* W, const void* R, void* O, const LnParams& p,
                             cudaStream_t st) {
   using G = LCfg<NF>;
-  static int max_pairs = 0;
+  static std::atomic<int> max_pairs_seen{0};
+  static std::atomic<uint64_t> configured{0};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  if (max_pairs == 0) {
+  once_per_device(configured, [&attr] {
     KH_CUDA(cudaFuncSetAttribute(gemm_addln_kernel<NF>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * device_sms(), 1, 1);
@@ -981,8 +984,9 @@ static void launch_addln_nf(const void* A, const void* W, const void* R, void* O
     int n = 0;
     KH_CUDA(cudaOccupancyMaxActiveClusters(&n, gemm_addln_kernel<NF>, &cfg));
     if (n <= 0) throw CudaError("gemm+layernorm: no CTA pair fits on the device");
-    max_pairs = n;
-  }
+    max_pairs_seen.store(n);  // the same on every B200
+  });
+  const int max_pairs = max_pairs_seen.load();
   const int M = p.M, K = p.K;
   const CUtensorMap& ma = tensor_map_f16(A, uint64_t(M), uint64_t(K), uint64_t(K), BK, BM, 128);
   const CUtensorMap& mb = tensor_map_f16(W, uint64_t(NF), uint64_t(K), uint64_t(K), BK, G::BQ, 128);

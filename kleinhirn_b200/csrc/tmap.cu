@@ -64,6 +64,19 @@ const CUtensorMap& tensor_map_f16(const void* ptr, uint64_t rows, uint64_t cols,
   return cache.emplace(key, m).first->second;
 }
 
+void once_per_device(std::atomic<uint64_t>& done, const std::function<void()>& configure) {
+  int dev = 0;
+  KH_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) throw ArgError("device ordinal above 63");
+  const uint64_t bit = 1ull << dev;
+  if (done.load(std::memory_order_acquire) & bit) return;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lk(mu);
+  if (done.load(std::memory_order_relaxed) & bit) return;
+  configure();
+  done.fetch_or(bit, std::memory_order_release);
+}
+
 int device_sms() {
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);

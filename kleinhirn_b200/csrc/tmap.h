@@ -1,6 +1,10 @@
 // TMA tensor maps of row-major f16 matrices (host side), cached by shape and pointer.
 #pragma once
 
+#include <atomic>
+#include <cstdint>
+#include <functional>
+
 #include <cuda.h>
 
 #include <cstdint>
@@ -17,5 +21,10 @@ void encode_tensor_map_f16(CUtensorMap* out, const void* ptr, uint64_t rows, uin
                            uint32_t box_cols, uint32_t box_rows, int swizzle_bytes);
 
 int device_sms();
+
+// Runs `configure` once per device (the current one) and process: kernel attributes such as the
+// shared-memory limit are per device, and several contexts of one process may drive different
+// devices from different host threads.
+void once_per_device(std::atomic<uint64_t>& done, const std::function<void()>& configure);
 
 }  // namespace kh
