@@ -48,8 +48,10 @@ enum kh_dtype { KH_F32 = 0, KH_F16 = 1 };
 /* Message of the last failure on this thread ("" when none). */
 const char* kh_last_error(void);
 
-/* Opens a context on the first of `devices` (n_devices >= 1). Replaces the device half of
- * loadBackend / loadGpu (src/backend.ts:75-89, src/webgpu-backend.ts:53-108). */
+/* Opens a context on devices[0]; n_devices must be 1 (KH_ERR_ARG otherwise: a context drives one
+ * device, and a host that uses several devices opens one context per device and drives each from
+ * its own thread). Replaces the device half of loadBackend / loadGpu (src/backend.ts:75-89,
+ * src/webgpu-backend.ts:53-108). */
 int kh_init(const int* devices, int n_devices, kh_ctx** out);
 
 /* Copies one weight tensor to the device: TensorDesc name, dtype (KH_F32 or KH_F16), shape
@@ -119,10 +121,12 @@ int kh_capture_check(const kh_plan* plan);
 int kh_run_capture(kh_plan* plan);
 int kh_read_capture(kh_plan* plan, float* out, size_t n);
 
-/* PlanRunner.destroy (src/backend.ts:27). */
+/* PlanRunner.destroy (src/backend.ts:27). Also destroys the plan's bulk handles that are still
+ * open; their handles are invalid afterwards. */
 void kh_plan_destroy(kh_plan* plan);
 
-/* Backend.dispose (src/backend.ts:45). */
+/* Backend.dispose (src/backend.ts:45). Also destroys the context's plans and bulk handles that
+ * are still open; their handles are invalid afterwards (a binding marks them destroyed). */
 void kh_destroy(kh_ctx* ctx);
 
 /* Backend.info (src/backend.ts:44): JSON with device name, SM count, memory, weight bytes.
@@ -194,6 +198,7 @@ int kh_bulk_last_timing(const kh_bulk* bulk, float* ms, int64_t* launches);
  * serialise the launches. */
 int kh_bulk_profile(kh_bulk* bulk, float* ms, size_t n);
 
+/* Frees a bulk handle (kh_plan_destroy and kh_destroy free the ones still open). */
 void kh_bulk_destroy(kh_bulk* bulk);
 
 /* The CUDA stream (cudaStream_t) every launch of this context goes to, so a caller can record
@@ -218,10 +223,39 @@ void* kh_ctx_stream(const kh_ctx* ctx);
  * The first call on a device does one-time set-up (looks up the static array, sets the kernel's
  * shared-memory limit): make that call before any stream capture. All calls on a device share
  * the static array: calls that overlap in time (other streams, other host threads) race on it,
- * so the caller serializes them. The work is queued on `stream` (a cudaStream_t, NULL for the
- * legacy default stream); the call returns once it is queued. */
+ * so the caller serializes them. The work is queued on `stream` (a cudaStream_t of the current
+ * device, NULL for the legacy default stream; a stream of another device is KH_ERR_ARG); the
+ * call returns once it is queued. seq_lens is read by a cudaMemcpyAsync on `stream`: from
+ * pageable host memory it has been read when the call returns, from page-locked memory it is
+ * read when the stream reaches the copy, so keep it unchanged until then.
+ * A wait of the kernel's pipeline that gives up (a lost arrival, after 2 s) ends the kernel early
+ * with ctx partly written and leaves a code on the device that this call cannot see, as the
+ * kernel runs after it returns: kh_attention_f16_noalloc_status reports it. */
 int kh_attention_f16_noalloc(const void* qkv, const float* mask, void* ctx, const int32_t* seq_lens, int n_seqs,
                              int heads, int head_dim, float scale, int window, void* stream);
+
+/* Waits for `stream` (as cudaStreamSynchronize) and reports whether an attention kernel on the
+ * current device gave up a pipeline wait since the last report: KH_OK, or KH_ERR_CUDA with the
+ * wait's code. Reading clears the code. Callers of kh_attention_f16_noalloc check it before they
+ * use ctx. (No counterpart in the reference.) */
+int kh_attention_f16_noalloc_status(void* stream);
+
+/* ---- failure-path self-tests (no counterpart in the reference) ----
+ * They make the failure on purpose, in the forms that leave the GPU usable, so the error
+ * handling of a context can be tested on a live device.
+ * kh_inject_cuda_error: the next entry point of ctx that latches errors reports a CUDA failure
+ *   named `what` (as if one of its CUDA calls had failed) and latches it, as failIfBroken does
+ *   (src/device.ts:79-81): every later call on ctx then fails with KH_ERR_STATE.
+ * kh_selftest_wait_limit: one CTA waits on an mbarrier nothing arrives on, with a limit of
+ *   limit_us microseconds (1 to 1e6); the wait gives up and records its code as a pipeline wait
+ *   that timed out does; the call synchronizes, returns KH_ERR_CUDA ("pipeline wait timed out")
+ *   and latches it in ctx.
+ * kh_selftest_tensor_maps: `threads` host threads (1-64) fetch `iters` TMA descriptors each from
+ *   the library's descriptor cache over more keys than it keeps; returns how many differ from a
+ *   fresh encoding (0 expected), or -1 on an error. */
+int kh_inject_cuda_error(kh_ctx* ctx, const char* what);
+int kh_selftest_wait_limit(kh_ctx* ctx, int limit_us);
+int64_t kh_selftest_tensor_maps(int threads, int iters);
 
 #ifdef __cplusplus
 }

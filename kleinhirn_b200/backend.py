@@ -1,8 +1,8 @@
 """CudaBackend: kleinhirn's ``Backend`` / ``PlanRunner`` interface (src/backend.ts:14-46) over the
 C ABI of libkhcuda.so (include/kh_cuda.h), through ctypes.
 
-This is the Python twin of the N-API binding a Node host would use (the TypeScript side is in
-INTEGRATION.md). Method names follow the reference interface in snake_case:
+This is the Python twin of the N-API binding a Node host would use. Method names follow the
+reference interface in snake_case:
 
     Backend.kind / weightBytes / check / runner / fitBatch / prepare / call / info / dispose
     PlanRunner.length / batch / markers / bytes / upload / run / readOutput / readCapture /
@@ -16,6 +16,7 @@ from __future__ import annotations
 
 import ctypes
 import json
+import weakref
 from pathlib import Path
 
 import numpy as np
@@ -69,6 +70,10 @@ _SIGS = {
     "kh_ctx_stream": ([_P], ctypes.c_void_p),
     "kh_attention_f16_noalloc": ([_P, _P, _P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float,
                                   ctypes.c_int, _P], ctypes.c_int),
+    "kh_attention_f16_noalloc_status": ([_P], ctypes.c_int),
+    "kh_inject_cuda_error": ([_P, ctypes.c_char_p], ctypes.c_int),
+    "kh_selftest_wait_limit": ([_P, ctypes.c_int], ctypes.c_int),
+    "kh_selftest_tensor_maps": ([ctypes.c_int, ctypes.c_int], ctypes.c_int64),
 }
 
 _lib = None
@@ -113,6 +118,22 @@ def attention_f16_noalloc(qkv_ptr: int, mask_ptr: int, ctx_ptr: int, seq_lens, h
                                               head_dim, scale, window, stream or None))
 
 
+def attention_f16_noalloc_status(stream: int = 0) -> None:
+    """kh_attention_f16_noalloc_status: waits for `stream`; raises KhError if an attention
+    pipeline wait on the current device gave up since the last report (the report clears it)."""
+    lib = load_library()
+    _check(lib, lib.kh_attention_f16_noalloc_status(stream or None))
+
+
+def selftest_tensor_maps(threads: int, iters: int) -> int:
+    """kh_selftest_tensor_maps: descriptors that differ from a fresh encoding (0 expected)."""
+    lib = load_library()
+    n = int(lib.kh_selftest_tensor_maps(threads, iters))
+    if n < 0:
+        raise KhError(3, lib.kh_last_error().decode("utf-8", "replace"))
+    return n
+
+
 def _ptr(a: np.ndarray | None):
     return None if a is None else ctypes.c_void_p(a.ctypes.data)
 
@@ -143,6 +164,8 @@ class CudaPlanRunner:
         self.markers = plan["markers"]
         self._bytes = nb.value
         self.f16 = plan["f16"]
+        self._bulks = weakref.WeakSet()  # open bulk handles: kh_plan_destroy frees them
+        backend._runners.add(self)
 
     @property
     def bytes(self) -> int:
@@ -222,7 +245,13 @@ class CudaPlanRunner:
     def destroy(self) -> None:
         if self.handle:
             self.lib.kh_plan_destroy(self.handle)
-            self.handle = None
+            self._forget()
+
+    def _forget(self) -> None:
+        """The library freed this plan (and its bulk handles): drop the handles."""
+        self.handle = None
+        for b in list(self._bulks):
+            b.handle = None
 
     def __del__(self):
         try:
@@ -243,6 +272,7 @@ class CudaBulk:
         self.handle = h
         self.n = 0
         self.tokens = 0
+        runner._bulks.add(self)
 
     def set_lengths(self, lens) -> None:
         a = np.ascontiguousarray(lens, dtype=np.int32)
@@ -307,9 +337,9 @@ class CudaBulk:
         return ms.value, n.value
 
     def close(self) -> None:
-        if self.handle:
+        if self.handle and self.runner.handle:
             self.lib.kh_bulk_destroy(self.handle)
-            self.handle = None
+        self.handle = None
 
     def __del__(self):
         try:
@@ -326,6 +356,7 @@ class CudaBackend:
 
     def __init__(self, tensors: dict[str, np.ndarray] | None = None, device: int = 0, lib_path=None):
         self.lib = load_library(lib_path)
+        self._runners = weakref.WeakSet()  # open plans: kh_destroy frees them
         devs = (ctypes.c_int * 1)(device)
         h = ctypes.c_void_p()
         _check(self.lib, self.lib.kh_init(devs, 1, ctypes.byref(h)))
@@ -391,15 +422,26 @@ class CudaBackend:
     def info(self) -> dict:
         return json.loads(_string(self.lib.kh_info, self.handle))
 
+    def inject_cuda_error(self, what: str) -> None:
+        """Failure-path self-test: the next latching call reports a CUDA failure named `what`."""
+        _check(self.lib, self.lib.kh_inject_cuda_error(self.handle, what.encode()))
+
+    def selftest_wait_limit(self, limit_us: int) -> None:
+        """Failure-path self-test: a bounded device wait gives up; raises the latched KhError."""
+        _check(self.lib, self.lib.kh_selftest_wait_limit(self.handle, int(limit_us)))
+
     @property
     def stream(self) -> int:
         """cudaStream_t of every launch of this backend (for caller-side CUDA events)."""
         return int(self.lib.kh_ctx_stream(self.handle) or 0)
 
     def dispose(self) -> None:
+        """Backend.dispose: frees the context with its plans and bulk handles still open."""
         if self.handle:
             self.lib.kh_destroy(self.handle)
             self.handle = None
+            for r in list(self._runners):
+                r._forget()
 
     def __del__(self):
         try:

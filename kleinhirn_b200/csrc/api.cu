@@ -4,6 +4,7 @@
 #include <algorithm>
 #include <cstring>
 #include <memory>
+#include <set>
 #include <sstream>
 #include <string>
 #include <vector>
@@ -12,15 +13,18 @@
 #include "attn_tc.h"
 #include "gemm_tc.h"
 #include "runtime.h"
+#include "tmap.h"
 
 using kh::Ctx;
 
 struct kh_ctx {
   std::unique_ptr<Ctx> c;
+  std::set<kh_plan*> plans;  // plans not yet destroyed: kh_destroy frees them
 };
 
 struct kh_plan {
   kh_ctx* owner = nullptr;
+  std::set<kh_bulk*> bulks;  // bulk handles not yet destroyed: kh_plan_destroy frees them
   kh::CompiledPlan cp;
   kh::Exec ex;
   std::vector<int32_t> htable;
@@ -72,6 +76,13 @@ int guard(Ctx* c, Latch latch, F&& f) {
       return KH_ERR_STATE;
     }
     if (c) KH_CUDA(cudaSetDevice(c->device));
+    if (c && latch == Latch::Yes && !c->inject.empty()) {
+      // a failure injected by kh_inject_cuda_error stands for a CUDA call of this entry point
+      // that failed: reported here, latched like a real one
+      const std::string what = "injected CUDA failure: " + c->inject;
+      c->inject.clear();
+      throw kh::CudaError(what);
+    }
     f();
     return KH_OK;
   } catch (const kh::CudaError& e) {
@@ -112,7 +123,8 @@ kh::SeqTable rebase(const kh::SeqTable& o, const int32_t* base) {
 }
 
 // A tensor-core pipeline wait that gave up leaves a code on the device; after a sync it becomes
-// a CUDA error of the call (and latches like one).
+// a CUDA error of the call (and latches like one). Reading clears the device's error words, so
+// the call that reads a code reports it and later contexts on the device start clean.
 void check_pipelines() {
   const int g = kh::tc_error_code();
   const int a = kh::attn_error_code();
@@ -154,6 +166,11 @@ int kh_init(const int* devices, int n_devices, kh_ctx** out) {
     return KH_ERR_ARG;
   }
   *out = nullptr;
+  if (n_devices > 1) {
+    g_err = "kh_init: a context drives one device; open one context per device (" + std::to_string(n_devices) +
+            " given)";
+    return KH_ERR_ARG;
+  }
   auto h = std::make_unique<kh_ctx>();
   h->c = std::make_unique<Ctx>();
   Ctx* c = h->c.get();
@@ -273,6 +290,7 @@ int kh_plan_create(kh_ctx* ctx, const char* plan_json, size_t len, kh_plan** out
     kh::exec_alloc(p->ex, c, &p->cp, rows, p->cp.batch, false);
   });
   if (st != KH_OK) return st;
+  ctx->plans.insert(p.get());
   *out = p.release();
   return KH_OK;
 }
@@ -474,6 +492,8 @@ void kh_plan_destroy(kh_plan* plan) {
   if (!plan) return;
   cudaSetDevice(plan->owner->c->device);
   cudaStreamSynchronize(plan->owner->c->stream);
+  for (kh_bulk* b : plan->bulks) delete b;  // the plan's bulk handles end with it
+  plan->owner->plans.erase(plan);
   delete plan;
 }
 
@@ -481,6 +501,11 @@ void kh_destroy(kh_ctx* ctx) {
   if (!ctx) return;
   cudaSetDevice(ctx->c->device);
   cudaStreamSynchronize(ctx->c->stream);
+  // plans and bulk handles still open end with the context (Backend.dispose, src/backend.ts:45)
+  for (kh_plan* p : ctx->plans) {
+    for (kh_bulk* b : p->bulks) delete b;
+    delete p;
+  }
   delete ctx;
 }
 
@@ -605,6 +630,7 @@ int kh_bulk_create(kh_plan* plan, int64_t max_tokens, int max_seqs, int64_t chun
     KH_CUDA(cudaEventCreate(&b->ev1));
   });
   if (st != KH_OK) return st;
+  plan->bulks.insert(b.get());
   *out = b.release();
   return KH_OK;
 }
@@ -884,6 +910,7 @@ void kh_bulk_destroy(kh_bulk* bulk) {
   if (!bulk) return;
   cudaSetDevice(bulk->plan->owner->c->device);
   cudaStreamSynchronize(bulk->plan->owner->c->stream);
+  bulk->plan->bulks.erase(bulk);
   delete bulk;
 }
 
@@ -893,6 +920,42 @@ int kh_attention_f16_noalloc(const void* qkv, const float* mask, void* ctx, cons
     kh::attention_f16_noalloc(qkv, mask, ctx, seq_lens, n_seqs, heads, head_dim, scale, window,
                               static_cast<cudaStream_t>(stream));
   });
+}
+
+int kh_attention_f16_noalloc_status(void* stream) {
+  return guard(nullptr, Latch::No, [&] {
+    const int code = kh::attention_status(static_cast<cudaStream_t>(stream));
+    if (code)
+      throw kh::CudaError("attention pipeline wait timed out (attention code " + std::to_string(code) + ")");
+  });
+}
+
+int kh_inject_cuda_error(kh_ctx* ctx, const char* what) {
+  if (!ctx || !what) {
+    g_err = "kh_inject_cuda_error: null argument";
+    return KH_ERR_ARG;
+  }
+  ctx->c->inject = *what ? what : "(unnamed)";
+  return KH_OK;
+}
+
+int kh_selftest_wait_limit(kh_ctx* ctx, int limit_us) {
+  if (!ctx) {
+    g_err = "kh_selftest_wait_limit: null context";
+    return KH_ERR_ARG;
+  }
+  Ctx* c = ctx->c.get();
+  return guard(c, Latch::Yes, [&] {
+    kh::launch_wait_limit_selftest(limit_us, c->stream);
+    KH_CUDA(cudaStreamSynchronize(c->stream));
+    check_pipelines();
+  });
+}
+
+int64_t kh_selftest_tensor_maps(int threads, int iters) {
+  int64_t bad = -1;
+  const int st = guard(nullptr, Latch::No, [&] { bad = kh::selftest_tensor_maps(threads, iters); });
+  return st == KH_OK ? bad : -1;
 }
 
 }  // extern "C"

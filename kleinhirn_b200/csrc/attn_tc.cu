@@ -725,7 +725,7 @@ __global__ void __launch_bounds__(128) relpos_tables_kernel(const __grid_constan
 // tile once for all its heads, and fewer, longer CTAs measured faster), an even number so both
 // softmax streams work; one head per CTA (split mode) for small launches.
 int heads_per_cta(int H, int tiles) {
-  static const int sms = device_sms();
+  const int sms = device_sms();  // of the current device
   for (int g = 12; g > 1; g -= 2)  // an even count keeps both softmax streams busy
     if (H % g == 0 && int64_t(tiles) * (H / g) >= int64_t(sms)) return g;
   return 1;  // one head per CTA: the two streams split its key tiles
@@ -850,9 +850,7 @@ __global__ void noalloc_rows_kernel(int32_t* w, int n, int T) {
 int32_t* noalloc_scratch() {
   static std::mutex mu;
   static int32_t* per_device[64] = {};
-  int dev = 0;
-  KH_CUDA(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= 64) throw ArgError("kh_attention_f16_noalloc: device ordinal above 63");
+  const int dev = current_device();
   std::lock_guard<std::mutex> lk(mu);
   if (!per_device[dev]) {
     void* ptr = nullptr;
@@ -892,6 +890,14 @@ void attention_f16_noalloc(const void* qkv, const float* mask, void* ctx, const 
   if (T > NA_MAX_ROWS)
     throw ArgError("kh_attention_f16_noalloc: " + std::to_string(T) + " packed rows, at most " +
                    std::to_string(NA_MAX_ROWS));
+  if (st) {
+    // the scratch address and the tensor maps below belong to the current device
+    int sdev = -1;
+    KH_CUDA(cudaStreamGetDevice(st, &sdev));
+    if (sdev != current_device())
+      throw ArgError("kh_attention_f16_noalloc: the stream belongs to device " + std::to_string(sdev) +
+                     ", the current device is " + std::to_string(current_device()));
+  }
   int32_t* w = noalloc_scratch();
   KH_CUDA(cudaMemcpyAsync(w + NA_LENS, seq_lens, size_t(n_seqs) * 4, cudaMemcpyHostToDevice, st));
   noalloc_starts_kernel<<<1, 1024, 0, st>>>(w, n_seqs);
@@ -952,9 +958,39 @@ void launch_attention(bool f16, const AttnArgs& a, const SeqTable& seq, cudaStre
 }
 
 int attn_error_code() {
+  // read and cleared (after a sync of the work that may have set it)
   int v = 0;
-  cudaMemcpyFromSymbol(&v, sm100::kh_tc_error, sizeof(int));
+  KH_CUDA(cudaMemcpyFromSymbol(&v, sm100::kh_tc_error, sizeof(int)));
+  if (v) {
+    const int zero = 0;
+    KH_CUDA(cudaMemcpyToSymbol(sm100::kh_tc_error, &zero, sizeof(int)));
+  }
   return v;
+}
+
+namespace {
+__global__ void wait_limit_selftest_kernel(unsigned long long limit_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    sm100::mbar_init(&bar, 1);
+    sm100::fence_barrier_init();
+  }
+  __syncthreads();
+  // nothing arrives on the barrier: the wait runs out after limit_ns and records code 90
+  if (threadIdx.x == 0) sm100::mbar_wait_for(&bar, 0, 90, limit_ns);
+  __syncthreads();
+}
+}  // namespace
+
+void launch_wait_limit_selftest(int limit_us, cudaStream_t st) {
+  if (limit_us < 1 || limit_us > 1000000) throw ArgError("wait-limit self-test: limit_us outside [1, 1e6]");
+  wait_limit_selftest_kernel<<<1, 32, 0, st>>>(1000ull * uint64_t(limit_us));
+  KH_CUDA(cudaGetLastError());
+}
+
+int attention_status(cudaStream_t st) {
+  KH_CUDA(cudaStreamSynchronize(st));
+  return attn_error_code();
 }
 
 }  // namespace kh

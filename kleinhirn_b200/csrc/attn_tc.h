@@ -16,12 +16,22 @@ void launch_attention(bool f16, const AttnArgs& a, const SeqTable& seq, cudaStre
 bool attention_tc_supported(bool f16, const AttnArgs& a);
 int64_t attention_rel_table_floats_per_row(int H, int np);
 
-// Code of the first tensor-core attention wait that gave up (0: none); read after a sync.
+// Code of the first tensor-core attention wait that gave up on the current device (0: none), read
+// after a sync and cleared, so the next call starts clean.
 int attn_error_code();
+
+// Failure-path self-test: one CTA waits, with a limit of limit_us microseconds, on an mbarrier
+// that nothing arrives on, so the wait gives up and records its code in the attention kernels'
+// error word, as a pipeline wait that timed out does. No copy or MMA is in flight.
+void launch_wait_limit_selftest(int limit_us, cudaStream_t st);
+
+// Synchronizes `st` and returns the attention error word of the current device (cleared).
+int attention_status(cudaStream_t st);
 
 // Packed f16 attention over caller-owned device buffers with the sequence table in static device
 // memory (kh_attention_f16_noalloc): qkv [T, 3 H D], mask [T] f32, ctx [T, H D]; seq_lens on the
-// host, T = their sum. Throws ArgError beyond its limits.
+// host, T = their sum. Throws ArgError beyond its limits, and when `st` belongs to another device
+// than the current one.
 void attention_f16_noalloc(const void* qkv, const float* mask, void* ctx, const int32_t* seq_lens, int n_seqs,
                            int H, int D, float scale, int window, cudaStream_t st);
 

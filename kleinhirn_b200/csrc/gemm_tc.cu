@@ -862,9 +862,11 @@ DevTensor gemm_geglu_bias(Ctx* ctx, const std::string& name, int N) {
 template <int BN, int MODE>
 static void launch_pair_mode(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const Params& p,
                              int tiles, cudaStream_t st) {
-  static std::atomic<int> max_pairs_seen{0};
+  // resident CTA pairs per device (contexts of one process may drive several devices)
+  static std::atomic<int> max_pairs_seen[64] = {};
   static std::atomic<uint64_t> configured{0};
-  once_per_device(configured, [] {
+  const int dev = current_device();
+  once_per_device(configured, [dev] {
     KH_CUDA(cudaFuncSetAttribute(gemm_pair_kernel<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  PCfg<BN>::SMEM));
     cudaLaunchConfig_t cfg = {};
@@ -881,9 +883,9 @@ static void launch_pair_mode(const CUtensorMap& ma, const CUtensorMap& mb, const
     int n = 0;
     KH_CUDA(cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<BN, MODE>, &cfg));
     if (n <= 0) throw CudaError("gemm: no CTA pair fits on the device");
-    max_pairs_seen.store(n);  // the same on every B200
+    max_pairs_seen[dev].store(n);
   });
-  const int pairs = std::min(tiles, max_pairs_seen.load());
+  const int pairs = std::min(tiles, max_pairs_seen[dev].load());
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -966,14 +968,16 @@ template <int NF>
 static void launch_addln_nf(const void* A, const void* W, const void* R, void* O, const LnParams& p,
                             cudaStream_t st) {
   using G = LCfg<NF>;
-  static std::atomic<int> max_pairs_seen{0};
+  // resident CTA pairs per device (contexts of one process may drive several devices)
+  static std::atomic<int> max_pairs_seen[64] = {};
   static std::atomic<uint64_t> configured{0};
+  const int dev = current_device();
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  once_per_device(configured, [&attr] {
+  once_per_device(configured, [&attr, dev] {
     KH_CUDA(cudaFuncSetAttribute(gemm_addln_kernel<NF>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * device_sms(), 1, 1);
@@ -984,9 +988,9 @@ static void launch_addln_nf(const void* A, const void* W, const void* R, void* O
     int n = 0;
     KH_CUDA(cudaOccupancyMaxActiveClusters(&n, gemm_addln_kernel<NF>, &cfg));
     if (n <= 0) throw CudaError("gemm+layernorm: no CTA pair fits on the device");
-    max_pairs_seen.store(n);  // the same on every B200
+    max_pairs_seen[dev].store(n);
   });
-  const int max_pairs = max_pairs_seen.load();
+  const int max_pairs = max_pairs_seen[dev].load();
   const int M = p.M, K = p.K;
   const CUtensorMap& ma = tensor_map_f16(A, uint64_t(M), uint64_t(K), uint64_t(K), BK, BM, 128);
   const CUtensorMap& mb = tensor_map_f16(W, uint64_t(NF), uint64_t(K), uint64_t(K), BK, G::BQ, 128);
@@ -1020,8 +1024,13 @@ void launch_gemm_addln(const void* A, const void* W, const void* bias, const voi
 }
 
 int tc_error_code() {
+  // read and cleared (after a sync of the work that may have set it)
   int v = 0;
-  cudaMemcpyFromSymbol(&v, sm100::kh_tc_error, sizeof(int));
+  KH_CUDA(cudaMemcpyFromSymbol(&v, sm100::kh_tc_error, sizeof(int)));
+  if (v) {
+    const int zero = 0;
+    KH_CUDA(cudaMemcpyToSymbol(sm100::kh_tc_error, &zero, sizeof(int)));
+  }
   return v;
 }
 

@@ -42,6 +42,7 @@ void launch_gemm_addln(const void* A, const void* W, const void* bias, const voi
 }  // namespace kh
 
 namespace kh {
-// Code of the first tensor-core pipeline wait that gave up (0: none); read after a sync.
+// Code of the first tensor-core pipeline wait of the GEMM kernels that gave up on the current
+// device (0: none), read after a sync and cleared, so the next call starts clean.
 int tc_error_code();
 }  // namespace kh

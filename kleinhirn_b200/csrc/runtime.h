@@ -50,6 +50,7 @@ struct Ctx {
   std::map<std::string, DevTensor> derived;  // dtype conversions and repacked layouts
   int64_t weight_bytes = 0;
   std::string broken;  // first CUDA error of a run: latched (src/device.ts:79-81)
+  std::string inject;  // a failure the next latching call reports (kh_inject_cuda_error)
   ~Ctx();
   // The tensor in storage type f16 (true) or f32, converted once on the device and cached.
   const DevTensor& weight(const std::string& name, bool f16);

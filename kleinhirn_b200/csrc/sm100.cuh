@@ -20,8 +20,9 @@
 namespace kh {
 namespace sm100 {
 
-// Error word of the tensor-core kernels of one translation unit: 0 ok, else the code of the
-// first wait that timed out (each .cu file that includes this header has its own copy).
+// Error word of the tensor-core kernels of one translation unit, one per device: 0 ok, else the
+// code of the first wait that timed out (each .cu file that includes this header has its own
+// copy). The host reads and clears it after a sync (the call that reads it reports the error).
 static __device__ int kh_tc_error = 0;
 
 constexpr unsigned long long WAIT_LIMIT_NS = 2000000000ull;  // 2 s for one wait
@@ -65,17 +66,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Waits for the phase with the given parity; false (and kh_tc_error = code) after the limit.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
+// Waits for the phase with the given parity; false (and kh_tc_error = code) after limit_ns.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, int code, unsigned long long limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 0 && global_ns() - t0 > WAIT_LIMIT_NS) {
+    if ((it & 255u) == 0 && global_ns() - t0 > limit_ns) {
       atomicCAS(&kh_tc_error, 0, code);
       return false;
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
+  return mbar_wait_for(bar, parity, code, WAIT_LIMIT_NS);
 }
 
 // 2-D TMA tile load into shared memory, completion on an mbarrier (no multicast).

@@ -1,9 +1,12 @@
 // TMA tensor-map encoding through the driver entry point, cached per (pointer, geometry).
 
+#include <cstring>
 #include <map>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <tuple>
+#include <vector>
 
 #include "runtime.h"
 #include "tmap.h"
@@ -50,8 +53,10 @@ void encode_tensor_map_f16(CUtensorMap* out, const void* ptr, uint64_t rows, uin
   if (r != CUDA_SUCCESS) throw CudaError("cuTensorMapEncodeTiled failed: " + std::to_string(int(r)));
 }
 
-const CUtensorMap& tensor_map_f16(const void* ptr, uint64_t rows, uint64_t cols, uint64_t row_stride,
-                                  uint32_t box_cols, uint32_t box_rows, int swizzle_bytes) {
+CUtensorMap tensor_map_f16(const void* ptr, uint64_t rows, uint64_t cols, uint64_t row_stride, uint32_t box_cols,
+                           uint32_t box_rows, int swizzle_bytes) {
+  // The map is copied out while the lock is held: another host thread (a context on another
+  // device) may clear the cache at any time after the lock is released.
   static std::mutex mu;
   static std::map<std::tuple<const void*, uint64_t, uint64_t, uint64_t, uint32_t, uint32_t, int>, CUtensorMap> cache;
   std::lock_guard<std::mutex> lk(mu);
@@ -61,7 +66,43 @@ const CUtensorMap& tensor_map_f16(const void* ptr, uint64_t rows, uint64_t cols,
   if (cache.size() > 8192) cache.clear();
   CUtensorMap m;
   encode_tensor_map_f16(&m, ptr, rows, cols, row_stride, box_cols, box_rows, swizzle_bytes);
-  return cache.emplace(key, m).first->second;
+  cache.emplace(key, m);
+  return m;
+}
+
+int64_t selftest_tensor_maps(int threads, int iters) {
+  // Threads fetch maps of distinct (pointer, geometry) keys, more than the cache keeps, so the
+  // cache is cleared while others hold their copies; every copy must equal a fresh encoding.
+  if (threads < 1 || threads > 64 || iters < 1 || iters > 100000)
+    throw ArgError("tensor-map self-test: threads in [1, 64], iters in [1, 1e5]");
+  void* base = nullptr;
+  KH_CUDA(cudaMalloc(&base, size_t(1) << 20));
+  std::atomic<int64_t> bad{0};
+  std::vector<std::thread> pool;
+  std::vector<std::string> errs(static_cast<size_t>(threads));
+  int dev = current_device();
+  for (int t = 0; t < threads; ++t)
+    pool.emplace_back([&, t] {
+      try {
+        KH_CUDA(cudaSetDevice(dev));
+        for (int i = 0; i < iters; ++i) {
+          const uint64_t off = uint64_t((t * 7919 + i * 104729) % 65000) * 16;
+          const char* p = static_cast<const char*>(base) + off;
+          const uint64_t rows = 64 + uint64_t((i + t) % 5);
+          const CUtensorMap m = tensor_map_f16(p, rows, 64, 64, 64, 64, 128);
+          CUtensorMap fresh;
+          encode_tensor_map_f16(&fresh, p, rows, 64, 64, 64, 64, 128);
+          if (std::memcmp(&m, &fresh, sizeof(CUtensorMap)) != 0) bad.fetch_add(1);
+        }
+      } catch (const std::exception& e) {
+        errs[size_t(t)] = e.what();
+      }
+    });
+  for (auto& th : pool) th.join();
+  cudaFree(base);
+  for (const auto& e : errs)
+    if (!e.empty()) throw CudaError("tensor-map self-test: " + e);
+  return bad.load();
 }
 
 void once_per_device(std::atomic<uint64_t>& done, const std::function<void()>& configure) {
@@ -78,10 +119,25 @@ void once_per_device(std::atomic<uint64_t>& done, const std::function<void()>& c
 }
 
 int device_sms() {
-  int dev = 0, sms = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  // SM count of the current device, looked up once per device (contexts of one process may drive
+  // devices with different counts from different host threads)
+  static std::atomic<int> sms_of[64] = {};
+  int dev = 0;
+  KH_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) throw ArgError("device ordinal above 63");
+  int sms = sms_of[dev].load(std::memory_order_relaxed);
+  if (sms <= 0) {
+    KH_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    sms_of[dev].store(sms, std::memory_order_relaxed);
+  }
   return sms;
+}
+
+int current_device() {
+  int dev = 0;
+  KH_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) throw ArgError("device ordinal above 63");
+  return dev;
 }
 
 }  // namespace kh

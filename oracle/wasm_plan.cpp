@@ -58,8 +58,22 @@ inline f4 vld(uint32_t p) { f4 v; std::memcpy(&v, MEM + p, 16); return v; }
 inline void vst(uint32_t p, f4 v) { std::memcpy(MEM + p, &v, 16); }
 inline f4 splat(float x) { return f4{x, x, x, x}; }
 inline float hsum(f4 v) { return v[0] + v[1] + v[2] + v[3]; }
-inline f4 vmin(f4 a, f4 b) { return f4{std::fmin(a[0], b[0]), std::fmin(a[1], b[1]), std::fmin(a[2], b[2]), std::fmin(a[3], b[3])}; }
-inline f4 vmax(f4 a, f4 b) { return f4{std::fmax(a[0], b[0]), std::fmax(a[1], b[1]), std::fmax(a[2], b[2]), std::fmax(a[3], b[3])}; }
+// WebAssembly f32.min / f32.max (and their f32x4 lanes, which AssemblyScript's Mathf.min / max
+// and f32x4.min / max compile to): a NaN operand gives NaN, and -0 < +0. std::fmin / fmax would
+// return the other operand for a NaN.
+// (selects, not branches: the compiler keeps the lanes in vector registers)
+inline float wmin(float a, float b) {
+  float r = a < b ? a : b;
+  r = a == b ? (std::signbit(a) ? a : b) : r;
+  return (a != a || b != b) ? a + b : r;  // a NaN operand: NaN
+}
+inline float wmax(float a, float b) {
+  float r = a > b ? a : b;
+  r = a == b ? (std::signbit(a) ? b : a) : r;
+  return (a != a || b != b) ? a + b : r;  // a NaN operand: NaN
+}
+inline f4 vmin(f4 a, f4 b) { return f4{wmin(a[0], b[0]), wmin(a[1], b[1]), wmin(a[2], b[2]), wmin(a[3], b[3])}; }
+inline f4 vmax(f4 a, f4 b) { return f4{wmax(a[0], b[0]), wmax(a[1], b[1]), wmax(a[2], b[2]), wmax(a[3], b[3])}; }
 inline f4 vfloor(f4 a) { return f4{std::floor(a[0]), std::floor(a[1]), std::floor(a[2]), std::floor(a[3])}; }
 inline f4 vabs(f4 a) { return f4{std::fabs(a[0]), std::fabs(a[1]), std::fabs(a[2]), std::fabs(a[3])}; }
 inline int32_t truncsat(float x) {
@@ -117,7 +131,7 @@ inline float gelu(float v) {
 
 // src/wasm/plan.ts:110-116
 float activate(float v, int act) {
-  if (act == 1) return std::fmax(v, 0.0f);
+  if (act == 1) return wmax(v, 0.0f);
   if (act == 2) return gelu(v);
   if (act == 3) return tanhf(v);
   if (act == 4) return v / (1.0f + expf(-v));
@@ -432,12 +446,12 @@ void pool(uint32_t x, uint32_t mask, uint32_t out, int L, int N, int mode, int b
         for (int d = 0; d < N; ++d) stf(o, d, ldf(o, d) + m * ldf(xr, d));
         cnt += m;
       } else if (m > 0.5f) {
-        for (int d = 0; d < N; ++d) stf(o, d, found ? std::fmax(ldf(o, d), ldf(xr, d)) : ldf(xr, d));
+        for (int d = 0; d < N; ++d) stf(o, d, found ? wmax(ldf(o, d), ldf(xr, d)) : ldf(xr, d));
         found = true;
       }
     }
     if (mode == 0) {
-      const float den = std::fmax(cnt, 1e-9f);
+      const float den = wmax(cnt, 1e-9f);
       for (int d = 0; d < N; ++d) stf(o, d, ldf(o, d) / den);
     }
   }
@@ -534,11 +548,11 @@ void softmaxRow(uint32_t p, int n, uint32_t mask, int first, int il, int window,
       vst(off(p, j), x);
       vm = vmax(vm, x);
     }
-    float m = std::fmax(std::fmax(vm[0], vm[1]), std::fmax(vm[2], vm[3]));
+    float m = wmax(wmax(vm[0], vm[1]), wmax(vm[2], vm[3]));
     for (; j < n; ++j) {
       const float x = ldf(p, j) * scale;
       stf(p, j, x);
-      m = std::fmax(m, x);
+      m = wmax(m, x);
     }
     const f4 vmx = splat(m);
     f4 vs = splat(0);
@@ -562,7 +576,7 @@ void softmaxRow(uint32_t p, int n, uint32_t mask, int first, int il, int window,
   }
   if (scale != 1) for (int j = 0; j < n; ++j) stf(p, j, ldf(p, j) * scale);
   float mx = LOWEST;
-  for (int j = 0; j < n; ++j) if (keep(mask, first + j, il, window)) mx = std::fmax(mx, ldf(p, j));
+  for (int j = 0; j < n; ++j) if (keep(mask, first + j, il, window)) mx = wmax(mx, ldf(p, j));
   float sum = 0;
   for (int j = 0; j < n; ++j) {
     float e = 0;

@@ -43,3 +43,14 @@ def test_init_without_device_returns_a_status():
     st = lib.kh_init(devs, 1, ctypes.byref(h))
     assert st != 0
     assert lib.kh_last_error().decode()
+
+
+def test_init_refuses_several_devices_in_one_context():
+    """A context drives one device: kh_init with two devices is an argument error, not a silent
+    drop of the second (a host that uses several devices opens one context per device)."""
+    lib = backend.load_library()
+    h = ctypes.c_void_p()
+    devs = (ctypes.c_int * 2)(0, 1)
+    assert lib.kh_init(devs, 2, ctypes.byref(h)) == 1
+    assert "one context per device" in lib.kh_last_error().decode()
+    assert not h.value

@@ -28,7 +28,11 @@ def test_contexts_on_two_devices_from_two_threads():
     ids = [np.minimum(x, 511) for x in synthetic.token_ids(name, lens, 3)]
     halves = [ids[0::2], ids[1::2]]
     # each half alone on device 0: the reference results
-    alone = [cuda_forward_bulk(CudaBackend(m.weights, device=0), m, h, 512, chunk_tokens=20000) for h in halves]
+    alone = []
+    for h in halves:
+        be0 = CudaBackend(m.weights, device=0)
+        alone.append(cuda_forward_bulk(be0, m, h, 512, chunk_tokens=20000))
+        be0.dispose()
     got: list = [None, None]
     errors: list = []
 
