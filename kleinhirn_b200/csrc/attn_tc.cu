@@ -93,6 +93,7 @@ struct Params {
   // and p2c = k . posQuery[p], and the plan's relative index relidx [L][L] (local positions)
   const float* rel_tables;
   const uint32_t* relidx;
+  const int32_t* rel1d;  // relidx as a function of i - j (null: use relidx)
   int L, NP;
 };
 
@@ -435,7 +436,43 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
         fence_before_sync();
         mbar_arrive(&s_empty[g]);  // S in TMEM is free for this stream's next item
         if constexpr (REL) {
-          // s = q.k + q.posKey[p] + k.posQuery[p], p = relidx[i][j] (local positions), over the kept keys
+          // s = q.k + q.posKey[p] + k.posQuery[p], p = relidx[i][j] (local positions)
+          if (p.rel1d) {
+            // p depends on i - j only: p = rel1d[row - kj + L - 1]. Every key of a chunk with a kept
+            // key gets the terms, four keys at a time with independent loads (for a fixed key the
+            // warp's rows read neighbouring table entries); addresses are clamped to the rows and
+            // the index range, and the scores of keys not kept are dropped to -inf below.
+            const int rowc = min(row, p.T - 1);
+            const float* c2p = p.rel_tables + (int64_t(rowc) * 2 * p.H + hg0 + hh) * p.NP;
+            const float* p2c0 = p.rel_tables + (int64_t(p.H) + hg0 + hh) * p.NP;  // row 0's p2c of this head
+            const int64_t rstride = int64_t(2) * p.H * p.NP;
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+              if (!__any_sync(0xffffffffu, km[c] != 0u)) continue;
+#pragma unroll
+              for (int g4 = 0; g4 < 32; g4 += 4) {
+                int pp[4];
+                int kc[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const int kj = k0 + c * 32 + g4 + e;
+                  kc[e] = min(kj, p.T - 1);
+                  pp[e] = __ldg(p.rel1d + min(max(row - kj + p.L - 1, 0), 2 * p.L - 2));
+                }
+                float a[4], b[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  a[e] = __ldg(c2p + pp[e]);
+                  b[e] = __ldg(p2c0 + int64_t(kc[e]) * rstride + pp[e]);
+                }
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const int i = c * 32 + g4 + e;
+                  sr[i] = __float_as_uint(__uint_as_float(sr[i]) + a[e] + b[e]);
+                }
+              }
+            }
+          } else {
           const float* c2p = p.rel_tables + (int64_t(row) * 2 * p.H + hg0 + hh) * p.NP;
           const uint32_t* ridx = p.relidx + int64_t(row - sstart) * p.L - sstart;
 #pragma unroll
@@ -450,6 +487,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
                 sr[c * 32 + i] = __float_as_uint(__uint_as_float(sr[c * 32 + i]) + __ldg(c2p + pp) + __ldg(p2c + pp));
               }
             }
+          }
           }
         }
         // warp-uniform cases per 32-key chunk: every lane keeps all keys, none keeps any, or mixed;
@@ -770,6 +808,7 @@ void launch_tc(const AttnArgs& a, const SeqTable& seq, int T, cudaStream_t st) {
   p.scale_log2 = a.scale * 1.4426950408889634f;
   p.rel_tables = a.rel_tables;
   p.relidx = a.relidx;
+  p.rel1d = a.rel1d;
   p.L = a.L;
   p.NP = a.np;
   dim3 grid(seq.nptiles, a.H / p.HG);

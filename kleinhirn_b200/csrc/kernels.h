@@ -85,6 +85,9 @@ struct AttnArgs {
   const void* pos_key = nullptr;
   const void* pos_query = nullptr;
   const uint32_t* relidx = nullptr;
+  // the same index as one row over i - j when it depends on i - j only (DeBERTa's relBucketIndex,
+  // src/plan/build.ts:22-45): rel1d[i - j + L - 1] == relidx[i][j]; null otherwise
+  const int32_t* rel1d = nullptr;
   int L = 0;           // bucket length: relidx is L x L
   int rows = 0;        // packed rows of the launch
   int np = 0;          // rows of pos_key / pos_query (relative positions)

@@ -365,12 +365,37 @@ void plan_compile(Ctx* ctx, const Json& plan, CompiledPlan& cp) {
       const void* pq = nullptr;
       int np = 0;
       bool rel_tables = false;
+      std::string rel1d_id;
       if (g.rel) {
         const DevTensor& tk = ctx->weight(g.pos_key.substr(2), f16);
         pk = tk.ptr;
         pq = ctx->weight(g.pos_query.substr(2), f16).ptr;
         np = tk.shape.empty() ? 0 : int(tk.shape[0]);
         use(g.relidx);
+        {
+          // relidx as one row over i - j, when the plan's L x L table depends on i - j only
+          const BufInfo& rb = touch(g.relidx);
+          const int L = g.L;
+          if (L > 0 && rb.init.size() >= size_t(L) * L * 4) {
+            const uint32_t* t = reinterpret_cast<const uint32_t*>(rb.init.data());
+            std::vector<int32_t> r1(size_t(2 * L - 1));
+            for (int d = 0; d < L; ++d) r1[size_t(d + L - 1)] = int32_t(t[size_t(d) * L]);    // i - j = d >= 0
+            for (int d = 1; d < L; ++d) r1[size_t(L - 1 - d)] = int32_t(t[size_t(d)]);        // i - j = -d
+            bool toeplitz = true;
+            for (int i = 0; i < L && toeplitz; ++i)
+              for (int j = 0; j < L; ++j)
+                if (int32_t(t[size_t(i) * L + j]) != r1[size_t(i - j + L - 1)]) { toeplitz = false; break; }
+            if (toeplitz) {
+              rel1d_id = "#rel1d:" + g.relidx;
+              BufInfo& b1 = touch(rel1d_id);
+              b1.kind = BufInfo::Fixed;
+              b1.elem = 4;
+              b1.init.resize(r1.size() * 4);
+              std::memcpy(b1.init.data(), r1.data(), b1.init.size());
+              b1.fixed_bytes = b1.init.size();
+            }
+          }
+        }
         AttnArgs probe;
         probe.rel = true; probe.D = g.D; probe.L = g.L; probe.np = np;
         if (attention_tc_supported(f16, probe)) {
@@ -385,6 +410,7 @@ void plan_compile(Ctx* ctx, const Json& plan, CompiledPlan& cp) {
       protos.push_back({"attention", g.names, [=](const CompiledPlan& c) {
         const int iq = bi(c, g.qkv), im = bi(c, g.mask), ic = bi(c, g.ctx);
         const int ir = g.rel ? bi(c, g.relidx) : -1;
+        const int i1 = rel1d_id.empty() ? -1 : bi(c, rel1d_id);
         const int it = rel_tables ? bi(c, "#reltables") : -1;
         Step s;
         s.run = [=](Exec& ex, cudaStream_t st) {
@@ -392,6 +418,7 @@ void plan_compile(Ctx* ctx, const Json& plan, CompiledPlan& cp) {
           a.qkv = ex.buf(iq); a.mask = (const float*)ex.buf(im); a.ctx = ex.buf(ic);
           a.H = g.H; a.D = g.D; a.scale = g.scale; a.window = g.window; a.rel = g.rel;
           a.pos_key = pk; a.pos_query = pq; a.relidx = ir >= 0 ? (const uint32_t*)ex.buf(ir) : nullptr;
+          a.rel1d = i1 >= 0 ? (const int32_t*)ex.buf(i1) : nullptr;
           a.L = g.L;
           a.np = np;
           a.rel_tables = it >= 0 ? (float*)ex.buf(it) : nullptr;

@@ -160,6 +160,33 @@ def test_relative_attention_f16(L, lens, span):
     assert np.all(err <= tol), f"worst {err.max()} at {int(np.argmax(err - tol))}"
 
 
+def test_relative_attention_index_not_a_function_of_distance():
+    """A relidx that does not depend on i - j alone (the plan builder's tables always do, but the
+    plan format allows any): the kernel reads the L x L table itself instead of folding it into a
+    row over i - j; against float64."""
+    L, lens, span = 200, [200, 90], 64
+    B, H, D = len(lens), 4, 64
+    hd = H * D
+    rng = np.random.default_rng(5)
+    qkv = (rng.standard_normal(B * L * 3 * hd) * 1.2).astype(np.float16)
+    mask = prefix_mask(L, lens)
+    for r in range(B * L):
+        if not mask[r]:
+            qkv[r * 3 * hd:(r + 1) * 3 * hd] = np.nan
+    i, j = np.meshgrid(np.arange(L), np.arange(L), indexing="ij")
+    idx = ((7 * i + 3 * j) % (2 * span)).astype(np.uint32).reshape(-1)
+    pk = (rng.standard_normal((2 * span, hd)) * 0.8).astype(np.float16)
+    pq = (rng.standard_normal((2 * span, hd)) * 0.8).astype(np.float16)
+    scale_div = math.sqrt(3 * D)
+    rows = B * L
+    want = relative_ref(qkv, mask, L, B, H, D, scale_div, idx, pk, pq)
+    got, _ = run_relative(qkv, mask, L, B, H, D, scale_div, idx, pk, pq, rows)
+    keep = np.repeat(mask[:rows] > 0, hd)
+    assert np.all(got[~keep] == 0)
+    err = np.abs(got[keep] - want[keep])
+    assert np.all(err <= 4e-3 + 1e-2 * np.abs(want[keep])), err.max()
+
+
 def standard_ref(qkv16, mask, L, B, H, D, scale, window):
     """attention_ref vectorised per (sequence, head), float64 (tests/wasm_plan.test.ts:299-333)."""
     x = qkv16.astype(np.float64).reshape(B, L, 3, H, D)
