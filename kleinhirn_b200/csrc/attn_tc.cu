@@ -66,9 +66,12 @@ struct Cfg {
   static constexpr int V_OFF = K_OFF + KS * KTILE;
   static constexpr int P_OFF = V_OFF + VS * KTILE;  // one P block per stream: 128 rows x 64 keys, 16 KB
   static constexpr int BITS_OFF = P_OFF + 2 * 16384;  // present-and-unmasked key bits [tile][2]
-  // D = 32: the row sums come from the tensor core (P times a ones tile, 16 columns of TMEM per
-  // stream next to O); D = 64 has no TMEM room left and sums in the softmax threads.
-  static constexpr bool SUMS = D == 32;
+  // Row sums from the tensor core (P times a ones tile, 16 columns of TMEM per stream next to O)
+  // instead of in the softmax threads: off. Each MMA instruction costs the issuing thread far
+  // more than its tensor-core time at these sizes (measured: about 60 cycles per instruction for
+  // M 128 x N 16..64 products), and the four sum MMAs per item measured 2.4 % slower overall
+  // than the softmax threads' own additions.
+  static constexpr bool SUMS = false;
   static constexpr int XCH_OFF = BITS_OFF + MAXKT * 2 * 4;  // split mode: m and l of both streams, f32 [2][2][128]
   static constexpr int LUT_OFF = XCH_OFF + 2 * 2 * 128 * 4;  // key masks of 4 bits as 4 words, [16]
   static constexpr int ONES_OFF = LUT_OFF + 16 * 16;
