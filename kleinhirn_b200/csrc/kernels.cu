@@ -6,6 +6,7 @@
 // with the row held in registers between the two LayerNorm passes (the variance is the mean of
 // (v - mean)^2, src/kernels/layernorm.wgsl:18-20).
 
+#include "act_f32.cuh"
 #include "kernels.h"
 #include "runtime.h"
 
@@ -30,24 +31,8 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-// GELU with the Abramowitz-Stegun 7.1.26 erf (src/kernels/mmtile.wgsl:22-31, the constants the
-// reference prints); exp through CUDA's expf.
-__device__ __forceinline__ float gelu_as(float v) {
-  const float u = v * 0.7071067811865476f;
-  const float t = 1.0f / (1.0f + 0.3275911f * fabsf(u));
-  const float p = (((((1.061405429f * t - 1.453152027f) * t) + 1.421413741f) * t - 0.284496736f) * t +
-                   0.254829592f) * t;
-  const float e = 1.0f - p * expf(-u * u);
-  return 0.5f * v * (1.0f + (v >= 0.0f ? e : -e));
-}
-
-__device__ __forceinline__ float activate(float v, int act) {
-  if (act == 1) return fmaxf(v, 0.0f);
-  if (act == 2) return gelu_as(v);
-  if (act == 3) return tanhf(v);
-  if (act == 4) return v / (1.0f + expf(-v));
-  return v;
-}
+using f32act::activate;
+using f32act::gelu_as;
 
 constexpr int MAXE = 32;  // elements per lane held in registers: N <= 1024
 
@@ -405,18 +390,20 @@ __global__ void im2col_kernel(const T* __restrict__ x, const float* __restrict__
   }
 }
 
-// C = act(A W^T + bias): 64 x 64 tiles, 256 threads with 4 x 4 outputs, k in steps of 16.
-template <typename T>
+// C = act(A W^T + bias): TS x TS tiles (64, or 32 when 64-wide tiles would leave SMs idle), 256
+// threads with (TS / 16) x (TS / 16) outputs each, k in steps of 16.
+template <typename T, int TS>
 __global__ void __launch_bounds__(256) gemm_simt_kernel(const T* __restrict__ A, const T* __restrict__ W,
                                                         const T* __restrict__ bias, T* __restrict__ C, int M, int N,
                                                         int K, int act) {
-  __shared__ float sa[16][64 + 1];
-  __shared__ float sw[16][64 + 1];
+  constexpr int R = TS / 16;  // outputs per thread in each direction
+  __shared__ float sa[16][TS + 1];
+  __shared__ float sw[16][TS + 1];
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
-  float acc[4][4] = {};
+  const int m0 = blockIdx.y * TS, n0 = blockIdx.x * TS;
+  float acc[R][R] = {};
   for (int k0 = 0; k0 < K; k0 += 16) {
-    for (int e = threadIdx.x; e < 64 * 16; e += 256) {
+    for (int e = threadIdx.x; e < TS * 16; e += 256) {
       const int r = e / 16, kk = e % 16;
       const int gm = m0 + r, gn = n0 + r, gk = k0 + kk;
       sa[kk][r] = (gm < M && gk < K) ? ld(A, int64_t(gm) * K + gk) : 0.f;
@@ -425,115 +412,104 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const T* __restrict__ A,
     __syncthreads();
 #pragma unroll
     for (int kk = 0; kk < 16; ++kk) {
-      float a[4], b[4];
+      float a[R], b[R];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) a[i] = sa[kk][ty * 4 + i];
+      for (int i = 0; i < R; ++i) a[i] = sa[kk][ty * R + i];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) b[j] = sw[kk][tx * 4 + j];
+      for (int j = 0; j < R; ++j) b[j] = sw[kk][tx * R + j];
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < R; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        for (int j = 0; j < R; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
     }
     __syncthreads();
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int gm = m0 + ty * 4 + i;
+  for (int i = 0; i < R; ++i) {
+    const int gm = m0 + ty * R + i;
     if (gm >= M) continue;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int gn = n0 + tx * 4 + j;
+    for (int j = 0; j < R; ++j) {
+      const int gn = n0 + tx * R + j;
       if (gn < N) st(C, int64_t(gm) * N + gn, activate(acc[i][j] + (bias ? ld(bias, gn) : 0.f), act));
     }
   }
 }
 
-// Attention on CUDA cores, flash form: one thread per query row (64 rows per CTA, one head),
-// keys in chunks of 32 through shared memory, online softmax in f32.
-constexpr int AQ = 64;
-constexpr int AK = 32;
+// Attention on CUDA cores, one warp per (query row, head): the lanes take the keys 32 at a time
+// (lane l the key j0 + l: its score, with DeBERTa's relative terms), the chunk enters an online
+// softmax in f32, and for the PV sum each lane owns the output dimensions l and l + 32. Keys with
+// mask 0, outside the window or past the sequence are skipped (their value rows may hold NaN).
+constexpr int AW = 16;          // warps (query rows) per CTA
+constexpr int AROWS_TILE = 64;  // rows of one work tile of the sequence table (attention_tile_q)
 
 template <typename T>
-__global__ void __launch_bounds__(AQ) attention_simt_kernel(AttnArgs a, SeqTable seq) {
-  const int tile = blockIdx.x;
+__global__ void __launch_bounds__(AW * 32) attention_simt_kernel(AttnArgs a, SeqTable seq) {
+  const int tile = blockIdx.x / (AROWS_TILE / AW), sub = blockIdx.x % (AROWS_TILE / AW);
   const int h = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int s = seq.tiles[2 * tile], q0 = seq.tiles[2 * tile + 1];
   const int base = seq.start[s], n = seq.len[s];
   const int H = a.H, D = a.D, hd = H * D;
   const T* qkv = static_cast<const T*>(a.qkv);
   T* ctx = static_cast<T*>(a.ctx);
-  __shared__ float sk[AK][64 + 1];
-  __shared__ float sv[AK][64 + 1];
-  __shared__ float skm[AK];
-  const int i = q0 + threadIdx.x;  // local query
-  const bool active = i < n;
+  __shared__ float sq[AW][64];
+  const int i = q0 + sub * AW + warp;  // local query
+  if (i >= n) return;                  // (warp-uniform)
   const int64_t qrow = int64_t(base) + i;
-  float q[64];
-  float acc[64];
-#pragma unroll
-  for (int d = 0; d < 64; ++d) {
-    q[d] = (active && d < D) ? ld(qkv, qrow * 3 * hd + int64_t(h) * D + d) : 0.f;
-    acc[d] = 0.f;
-  }
-  const bool qvalid = active && a.mask[qrow] > 0.5f;
-  float m = -3.40282346638528859812e38f, l = 0.f;
+  for (int d = lane; d < D; d += 32) sq[warp][d] = ld(qkv, qrow * 3 * hd + int64_t(h) * D + d);
+  __syncwarp();
+  const float* q = sq[warp];
+  const bool qvalid = a.mask[qrow] > 0.5f;
   const T* pk = static_cast<const T*>(a.pos_key);
   const T* pq = static_cast<const T*>(a.pos_query);
-  for (int j0 = 0; j0 < n; j0 += AK) {
-    __syncthreads();
-    for (int e = threadIdx.x; e < AK * D; e += AQ) {
-      const int jj = e / D, d = e % D;
-      const int j = j0 + jj;
-      float kv = 0.f, vv = 0.f;
-      if (j < n) {
-        const int64_t kr = int64_t(base + j) * 3 * hd;
-        kv = ld(qkv, kr + int64_t(H + h) * D + d);
-        vv = ld(qkv, kr + int64_t(2 * H + h) * D + d);
-      }
-      sk[jj][d] = kv;
-      sv[jj][d] = vv;
-    }
-    for (int jj = threadIdx.x; jj < AK; jj += AQ) {
-      const int j = j0 + jj;
-      skm[jj] = (j < n && a.mask[base + j] > 0.5f) ? 1.f : 0.f;
-    }
-    __syncthreads();
-    if (!qvalid) continue;
-    for (int jj = 0; jj < AK; ++jj) {
-      const int j = j0 + jj;
-      if (j >= n || skm[jj] == 0.f) continue;
-      if (a.window && abs(i - j) > a.window) continue;
-      float sc = 0.f;
-#pragma unroll
-      for (int d = 0; d < 64; ++d)
-        if (d < D) sc += q[d] * sk[jj][d];
+  float m = -3.40282346638528859812e38f, l = 0.f, acc0 = 0.f, acc1 = 0.f;
+  for (int j0 = 0; qvalid && j0 < n; j0 += 32) {
+    const int j = j0 + lane;
+    const bool keep = j < n && a.mask[base + j] > 0.5f && !(a.window && abs(i - j) > a.window);
+    float sc = -INFINITY;
+    if (keep) {
+      const int64_t kr = int64_t(base + j) * 3 * hd + int64_t(H + h) * D;
+      float dot = 0.f;
+      for (int d = 0; d < D; ++d) dot += q[d] * ld(qkv, kr + d);
       if (a.rel) {
-        const int64_t p = a.relidx[int64_t(i) * a.L + j];
+        const int64_t pp = a.relidx[int64_t(i) * a.L + j];
         float c2p = 0.f, p2c = 0.f;
         for (int d = 0; d < D; ++d) {
-          c2p += q[d] * ld(pk, p * hd + int64_t(h) * D + d);
-          p2c += sk[jj][d] * ld(pq, p * hd + int64_t(h) * D + d);
+          c2p += q[d] * ld(pk, pp * hd + int64_t(h) * D + d);
+          p2c += ld(qkv, kr + d) * ld(pq, pp * hd + int64_t(h) * D + d);
         }
-        sc = (sc + c2p + p2c) * a.scale;
+        sc = (dot + c2p + p2c) * a.scale;
       } else {
-        sc *= a.scale;
+        sc = dot * a.scale;
       }
-      const float mn = fmaxf(m, sc);
-      const float corr = expf(m - mn);
-      const float pexp = expf(sc - mn);
-      l = l * corr + pexp;
-#pragma unroll
-      for (int d = 0; d < 64; ++d)
-        if (d < D) acc[d] = acc[d] * corr + pexp * sv[jj][d];
-      m = mn;
     }
-  }
-  if (!active) return;
-  const float invl = (qvalid && l > 0.f) ? 1.0f / l : 0.f;
+    float cmax = sc;
 #pragma unroll
-  for (int d = 0; d < 64; ++d)
-    if (d < D) st(ctx, qrow * hd + int64_t(h) * D + d, acc[d] * invl);
+    for (int o = 16; o > 0; o >>= 1) cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, o));
+    if (cmax == -INFINITY) continue;  // no kept key in this chunk
+    const float mn = fmaxf(m, cmax);
+    const float corr = expf(m - mn);
+    const float pe = keep ? expf(sc - mn) : 0.f;
+    float psum = pe;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
+    l = l * corr + psum;
+    acc0 *= corr;
+    acc1 *= corr;
+    const int nj = min(32, n - j0);
+    for (int jj = 0; jj < nj; ++jj) {
+      const float pj = __shfl_sync(0xffffffffu, pe, jj);
+      if (pj == 0.f) continue;  // a key not kept (or with no weight): its value row stays out
+      const int64_t vr = int64_t(base + j0 + jj) * 3 * hd + int64_t(2 * H + h) * D;
+      if (lane < D) acc0 += pj * ld(qkv, vr + lane);
+      if (lane + 32 < D) acc1 += pj * ld(qkv, vr + lane + 32);
+    }
+    m = mn;
+  }
+  const float invl = (qvalid && l > 0.f) ? 1.0f / l : 0.f;
+  if (lane < D) st(ctx, qrow * hd + int64_t(h) * D + lane, acc0 * invl);
+  if (lane + 32 < D) st(ctx, qrow * hd + int64_t(h) * D + lane + 32, acc1 * invl);
 }
 
 __global__ void f32_to_f16_kernel(const float* src, __half* dst, int64_t n) {
@@ -685,21 +661,32 @@ void launch_im2col(bool f16, const void* x, const float* mask, void* out, int N,
 void launch_gemm_simt(bool f16, const void* A, const void* W, const void* bias, void* C, int M, int N, int K, int act,
                       cudaStream_t st) {
   if (M <= 0 || N <= 0) return;
-  dim3 grid((N + 63) / 64, (M + 63) / 64);
-  if (f16)
-    gemm_simt_kernel<__half><<<grid, 256, 0, st>>>((const __half*)A, (const __half*)W, (const __half*)bias,
-                                                   (__half*)C, M, N, K, act);
-  else
-    gemm_simt_kernel<float><<<grid, 256, 0, st>>>((const float*)A, (const float*)W, (const float*)bias, (float*)C, M,
-                                                  N, K, act);
+  const int64_t tiles64 = int64_t((N + 63) / 64) * ((M + 63) / 64);
+  if (tiles64 >= 2 * 148) {
+    dim3 grid((N + 63) / 64, (M + 63) / 64);
+    if (f16)
+      gemm_simt_kernel<__half, 64><<<grid, 256, 0, st>>>((const __half*)A, (const __half*)W, (const __half*)bias,
+                                                         (__half*)C, M, N, K, act);
+    else
+      gemm_simt_kernel<float, 64><<<grid, 256, 0, st>>>((const float*)A, (const float*)W, (const float*)bias,
+                                                        (float*)C, M, N, K, act);
+  } else {  // small launches (B = 1 calls): four times the CTAs
+    dim3 grid((N + 31) / 32, (M + 31) / 32);
+    if (f16)
+      gemm_simt_kernel<__half, 32><<<grid, 256, 0, st>>>((const __half*)A, (const __half*)W, (const __half*)bias,
+                                                         (__half*)C, M, N, K, act);
+    else
+      gemm_simt_kernel<float, 32><<<grid, 256, 0, st>>>((const float*)A, (const float*)W, (const float*)bias,
+                                                        (float*)C, M, N, K, act);
+  }
 }
 
 void launch_attention_simt(bool f16, const AttnArgs& a, const SeqTable& seq, cudaStream_t st) {
   if (a.D > 64) throw std::runtime_error("attention: head dimension above 64");
   if (seq.ntiles <= 0) return;
-  dim3 grid(seq.ntiles, a.H);
-  if (f16) attention_simt_kernel<__half><<<grid, AQ, 0, st>>>(a, seq);
-  else attention_simt_kernel<float><<<grid, AQ, 0, st>>>(a, seq);
+  dim3 grid(seq.ntiles * (AROWS_TILE / AW), a.H);
+  if (f16) attention_simt_kernel<__half><<<grid, AW * 32, 0, st>>>(a, seq);
+  else attention_simt_kernel<float><<<grid, AW * 32, 0, st>>>(a, seq);
 }
 
 void launch_f32_to_f16(const float* src, __half* dst, int64_t n, cudaStream_t st) {
