@@ -12,6 +12,7 @@
 #include "../../include/kh_cuda.h"
 #include "attn_tc.h"
 #include "gemm_tc.h"
+#include "gemm_tf32.h"
 #include "runtime.h"
 #include "tmap.h"
 
@@ -128,9 +129,10 @@ kh::SeqTable rebase(const kh::SeqTable& o, const int32_t* base) {
 void check_pipelines() {
   const int g = kh::tc_error_code();
   const int a = kh::attn_error_code();
-  if (g || a)
+  const int f = kh::tf32_error_code();
+  if (g || a || f)
     throw kh::CudaError("tensor-core pipeline wait timed out (gemm code " + std::to_string(g) + ", attention code " +
-                        std::to_string(a) + ")");
+                        std::to_string(a) + ", f32 gemm code " + std::to_string(f) + ")");
 }
 
 std::string json_escape(const std::string& s) {

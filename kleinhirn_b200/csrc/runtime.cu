@@ -22,6 +22,7 @@
 #include <sstream>
 
 #include "gemm_tc.h"
+#include "gemm_tf32.h"
 #include "attn_tc.h"
 #include "runtime.h"
 
@@ -468,6 +469,36 @@ void plan_compile(Ctx* ctx, const Json& plan, CompiledPlan& cp) {
           names.push_back(nx["name"].as_str());
           written(nx);
         }
+      }
+      if (!f16 && gemm_tf32_supported(N, K)) {
+        // f32 plans on the tensor cores: A split into TF32 hi + lo parts (scratch rows of this
+        // runtime), the weight's split derived once, three TF32 products per K step
+        const float* wsplit = static_cast<const float*>(gemm_tf32_weight(ctx, wname).ptr);
+        const int64_t wn = int64_t(N) * K;
+        for (const char* id : {"#tf32hi", "#tf32lo"}) {
+          BufInfo& sb = touch(id);
+          sb.kind = BufInfo::Rows;
+          sb.elem = 4;
+          sb.cols = std::max<int64_t>(sb.cols, K);
+        }
+        written(op);
+        protos.push_back({"gemm", names, [=](const CompiledPlan& c) {
+          const int ia = bi(c, a_id), io = bi(c, out_id), ih = bi(c, "#tf32hi"), il = bi(c, "#tf32lo");
+          auto fb = resolve(c, bias);
+          const bool bias_zero = !bias.weight;
+          Step s;
+          s.launches = 2;
+          s.run = [=](Exec& ex, cudaStream_t st) {
+            const int M = fixed_rows ? (ex.bulk ? ex.seq.count : fixed_m) : ex.T;
+            float* hi = static_cast<float*>(ex.buf(ih));
+            float* lo = static_cast<float*>(ex.buf(il));
+            launch_tf32_split(static_cast<const float*>(ex.buf(ia)), hi, lo, int64_t(M) * K, st);
+            launch_gemm_tf32x3(hi, lo, wsplit, wsplit + wn, bias_zero ? nullptr : static_cast<const float*>(fb(ex)),
+                               static_cast<float*>(ex.buf(io)), M, N, K, act, st);
+          };
+          return s;
+        }});
+        continue;
       }
       if (addln) {
         protos.push_back({"gemm", names, [=](const CompiledPlan& c) {

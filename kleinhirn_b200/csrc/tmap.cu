@@ -35,22 +35,45 @@ EncodeTiled encode_fn() {
 
 }  // namespace
 
-void encode_tensor_map_f16(CUtensorMap* out, const void* ptr, uint64_t rows, uint64_t cols, uint64_t row_stride,
-                           uint32_t box_cols, uint32_t box_rows, int swizzle_bytes) {
-  if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (row_stride * 2) % 16)
+namespace {
+void encode_2d(CUtensorMap* out, CUtensorMapDataType dtype, uint64_t esize, const void* ptr, uint64_t rows,
+               uint64_t cols, uint64_t row_stride, uint32_t box_cols, uint32_t box_rows, int swizzle_bytes) {
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (row_stride * esize) % 16)
     throw PlanError("tensor map: base or row stride not 16-byte aligned");
   const cuuint64_t dims[2] = {cols, rows};
-  const cuuint64_t strides[1] = {row_stride * 2};
+  const cuuint64_t strides[1] = {row_stride * esize};
   const cuuint32_t box[2] = {box_cols, box_rows};
   const cuuint32_t estr[2] = {1, 1};
   const CUtensorMapSwizzle sw = swizzle_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
                                 : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
                                 : swizzle_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
                                                       : CU_TENSOR_MAP_SWIZZLE_NONE;
-  const CUresult r = encode_fn()(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
+  const CUresult r = encode_fn()(out, dtype, 2, const_cast<void*>(ptr), dims, strides, box,
                                  estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) throw CudaError("cuTensorMapEncodeTiled failed: " + std::to_string(int(r)));
+}
+}  // namespace
+
+void encode_tensor_map_f16(CUtensorMap* out, const void* ptr, uint64_t rows, uint64_t cols, uint64_t row_stride,
+                           uint32_t box_cols, uint32_t box_rows, int swizzle_bytes) {
+  encode_2d(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, ptr, rows, cols, row_stride, box_cols, box_rows, swizzle_bytes);
+}
+
+CUtensorMap tensor_map_f32(const void* ptr, uint64_t rows, uint64_t cols, uint64_t row_stride, uint32_t box_cols,
+                           uint32_t box_rows) {
+  // (f32 operands of the 3xTF32 GEMM: 128-byte swizzle; cached and copied out like the f16 maps)
+  static std::mutex mu;
+  static std::map<std::tuple<const void*, uint64_t, uint64_t, uint64_t, uint32_t, uint32_t>, CUtensorMap> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  const auto key = std::make_tuple(ptr, rows, cols, row_stride, box_cols, box_rows);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  if (cache.size() > 8192) cache.clear();
+  CUtensorMap m;
+  encode_2d(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ptr, rows, cols, row_stride, box_cols, box_rows, 128);
+  cache.emplace(key, m);
+  return m;
 }
 
 CUtensorMap tensor_map_f16(const void* ptr, uint64_t rows, uint64_t cols, uint64_t row_stride, uint32_t box_cols,

@@ -16,7 +16,11 @@ namespace kh {
 CUtensorMap tensor_map_f16(const void* ptr, uint64_t rows, uint64_t cols, uint64_t row_stride, uint32_t box_cols,
                            uint32_t box_rows, int swizzle_bytes);
 
-// The same map encoded into `out`, without the cache.
+// Map of a row-major f32 matrix (128-byte swizzle, zero fill outside), cached like the f16 maps.
+CUtensorMap tensor_map_f32(const void* ptr, uint64_t rows, uint64_t cols, uint64_t row_stride, uint32_t box_cols,
+                           uint32_t box_rows);
+
+// The f16 map encoded into `out`, without the cache.
 void encode_tensor_map_f16(CUtensorMap* out, const void* ptr, uint64_t rows, uint64_t cols, uint64_t row_stride,
                            uint32_t box_cols, uint32_t box_rows, int swizzle_bytes);
 
