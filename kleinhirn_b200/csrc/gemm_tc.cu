@@ -499,10 +499,12 @@ __global__ void __launch_bounds__(PCfg<BN>::THREADS, 1)
 // ffnOut + lnF) in one kernel. A pair owns whole 256-row tiles (all NF columns): two MMAs per
 // K = 16 step, N = NF / 2 each, accumulate into TMEM columns [0, NF/2) and [256, 256 + NF/2); each
 // CTA stages its 128 rows of the residual R by TMA into shared memory, and 16 epilogue warps
-// (four column quarters per TMEM lane quarter) take three passes over the accumulator: the row
-// sum, the sum of squared deviations (the reference's two-pass variance,
-// src/kernels/layernorm.wgsl:18-20), then the normalized f16 row, written over the staged R and
-// stored by TMA. One accumulator: the next tile's MMAs wait until the last pass has read it.
+// (four column quarters per TMEM lane quarter) take three passes over their rows: (1) y =
+// f16(acc + bias) from the accumulator into registers (packed halves, 48 per thread at NF 384)
+// and the row sum of v = y + R; (2) the sum of squared deviations (the reference's two-pass
+// variance, src/kernels/layernorm.wgsl:18-20); (3) the normalized f16 row, written over the
+// staged R and stored by TMA. Passes 2 and 3 recompute v from y and R (exact: the same f32 sum),
+// so the one accumulator is released after pass 1 and the next tile's MMAs run under them.
 template <int NF>
 struct LCfg {
   static constexpr int NH = NF / 2;                 // N of each of the two MMAs
@@ -675,40 +677,49 @@ __global__ void __launch_bounds__(LCfg<NF>::THREADS, 1)
     bool res_pending = false;
     int local = 0;
     auto tcol = [&](int c0) { return trow + uint32_t(c0 < G::NH ? c0 : c0 - G::NH + G::D1); };
-    // v = round(acc + bias) + R for the 32 columns c0 .. c0 + 31 of row r, from the accumulator
-    auto make_v = [&](int c0, float (&v)[32]) {
-      uint32_t a[32];
-      tmem_ld32(tcol(c0), a);
-      tmem_ld_wait();
-      const float4* bs = reinterpret_cast<const float4*>(vbias + c0);
-#pragma unroll
-      for (int i4 = 0; i4 < 8; ++i4) {
-        const float4 b4 = bs[i4];
-        v[4 * i4] = __uint_as_float(a[4 * i4]) + b4.x;
-        v[4 * i4 + 1] = __uint_as_float(a[4 * i4 + 1]) + b4.y;
-        v[4 * i4 + 2] = __uint_as_float(a[4 * i4 + 2]) + b4.z;
-        v[4 * i4 + 3] = __uint_as_float(a[4 * i4 + 3]) + b4.w;
-      }
+    constexpr int NP = QC / 16;   // 16-column pieces of a quarter: 4 or 6
+    constexpr int NT = 4;         // pieces kept in TMEM
+    constexpr int NR = NP - NT;   // pieces kept in registers: 0 or 2
+    // y = f16(acc + bias) of this thread's row and quarter (packed halves, 8 words a piece) is
+    // kept from pass 1 to pass 3: pieces 0-3 in the TMEM columns the accumulators leave free
+    // (32 per quarter: [NF/2, 256) and [256 + NF/2, 512)), the rest in registers. The accumulator
+    // is released after pass 1 and the next tile's MMAs run under the LayerNorm passes (v = y + R
+    // is recomputed exactly from y and the staged R).
+    const uint32_t ybase =
+        trow + uint32_t(NF == 256 ? 128 + g * 32 : (g < 2 ? 192 + g * 32 : 448 + (g - 2) * 32));
+    uint32_t yr[NR > 0 ? NR : 1][8];
+    // v = y + R, f32, of the 16 columns of piece k (R from the staged residual)
+    auto make_v = [&](int k, const uint32_t (&yk)[8], float (&v)[16]) {
+      const int c0 = g * QC + k * 16;
       const uint8_t* xrow = sX + (c0 >> 6) * OUT_BYTES + r * 128;
       const int ch0 = (c0 & 63) >> 3;
 #pragma unroll
-      for (int cq = 0; cq < 4; ++cq) {
+      for (int cq = 0; cq < 2; ++cq) {
         const uint4 u = *reinterpret_cast<const uint4*>(xrow + (((ch0 + cq) ^ (r & 7)) * 16));
-        const __half2* h = reinterpret_cast<const __half2*>(&u);
+        const uint32_t rw[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float2 f = __half22float2(h[e]);
-          v[cq * 8 + 2 * e] = f16r(v[cq * 8 + 2 * e]) + f.x;
-          v[cq * 8 + 2 * e + 1] = f16r(v[cq * 8 + 2 * e + 1]) + f.y;
+          const uint32_t yw = yk[cq * 4 + e];
+          const float2 s = fadd2(__half22float2(*reinterpret_cast<const __half2*>(&yw)),
+                                 __half22float2(*reinterpret_cast<const __half2*>(&rw[e])));
+          v[cq * 8 + 2 * e] = s.x;
+          v[cq * 8 + 2 * e + 1] = s.y;
         }
       }
     };
-    auto load_v = [&](int c0, float (&v)[32]) {
-      uint32_t a[32];
-      tmem_ld32(tcol(c0), a);
-      tmem_ld_wait();
+    // y of two pieces k0, k0 + 1 (one TMEM wait for both)
+    auto load_y2 = [&](int k0, uint32_t (&y0)[8], uint32_t (&y1)[8]) {
+      if (k0 < NT) {
+        tmem_ld8(ybase + uint32_t(k0 * 8), y0);
+        tmem_ld8(ybase + uint32_t(k0 * 8 + 8), y1);
+        tmem_ld_wait();
+      } else {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(a[i]);
+        for (int i = 0; i < 8; ++i) {
+          y0[i] = yr[k0 - NT][i];
+          y1[i] = yr[k0 + 1 - NT][i];
+        }
+      }
     };
     for (int t = pair; t < tiles; t += npairs, ++local) {
       const int row0 = t * 2 * BM + int(rank) * BM;
@@ -727,64 +738,100 @@ __global__ void __launch_bounds__(LCfg<NF>::THREADS, 1)
         break;
       }
       fence_after_sync();
-      // pass 1: v into the accumulator's columns (f32), and the row sum
-      float s = 0.f;
-#pragma unroll 1
-      for (int cc = 0; cc < QC / 32; ++cc) {
-        const int c0 = g * QC + cc * 32;
-        float v[32];
-        make_v(c0, v);
+      // pass 1: y from the accumulator, and this thread's statistics of v over its QC columns:
+      // sums of d = v - c and d^2 around c = its first v (shifted sums, no cancellation to speak
+      // of), merged over the four column quarters below (Chan, Golub and LeVeque's pairwise
+      // update of means and squared deviations)
+      float2 s2 = make_float2(0.f, 0.f), q2 = make_float2(0.f, 0.f);
+      float c = 0.f;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) s += v[i];
-        tmem_st32(tcol(c0), *reinterpret_cast<uint32_t(*)[32]>(v));
+      for (int k = 0; k < NP; ++k) {
+        const int c0 = g * QC + k * 16;
+        uint32_t yk[8];
+        {
+          uint32_t a[16];
+          tmem_ld16(tcol(c0), a);
+          tmem_ld_wait();
+          const float4* bs = reinterpret_cast<const float4*>(vbias + c0);
+#pragma unroll
+          for (int i4 = 0; i4 < 4; ++i4) {
+            const float4 b4 = bs[i4];
+            const float2 p0 = fadd2(make_float2(__uint_as_float(a[4 * i4]), __uint_as_float(a[4 * i4 + 1])),
+                                    make_float2(b4.x, b4.y));
+            const float2 p1 = fadd2(make_float2(__uint_as_float(a[4 * i4 + 2]), __uint_as_float(a[4 * i4 + 3])),
+                                    make_float2(b4.z, b4.w));
+            const __half2 h0 = __floats2half2_rn(p0.x, p0.y), h1 = __floats2half2_rn(p1.x, p1.y);
+            yk[2 * i4] = *reinterpret_cast<const uint32_t*>(&h0);
+            yk[2 * i4 + 1] = *reinterpret_cast<const uint32_t*>(&h1);
+          }
+        }
+        if (k < NT) {
+          tmem_st8(ybase + uint32_t(k * 8), yk);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) yr[k - NT][i] = yk[i];
+        }
+        float v[16];
+        make_v(k, yk, v);
+        if (k == 0) c = v[0];
+        const float2 nc = make_float2(-c, -c);
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) {
+          const float2 d = fadd2(make_float2(v[i], v[i + 1]), nc);
+          s2 = fadd2(s2, d);
+          q2 = ffma2(d, d, q2);
+        }
       }
+      // the accumulator is read (and y stored): the MMAs of the next tile may start
       tmem_st_wait();
-      red1[g * 128 + r] = s;
-      named_bar(1, 512);
-      const float mean = ((red1[r] + red1[128 + r]) + (red1[256 + r] + red1[384 + r])) / float(NF);
-      // pass 2: squared deviations
-      float qs = 0.f;
-#pragma unroll 1
-      for (int cc = 0; cc < QC / 32; ++cc) {
-        float v[32];
-        load_v(g * QC + cc * 32, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float d = v[i] - mean;
-          qs += d * d;
-        }
-      }
-      red2[g * 128 + r] = qs;
-      named_bar(1, 512);
-      const float var = ((red2[r] + red2[128 + r]) + (red2[256 + r] + red2[384 + r])) / float(NF);
-      const float inv = 1.0f / sqrtf(var + p.eps);
-      // pass 3: (v - mean) inv w + b, over the staged residual
-#pragma unroll 1
-      for (int cc = 0; cc < QC / 32; ++cc) {
-        const int c0 = g * QC + cc * 32;
-        float v[32];
-        load_v(c0, v);
-        uint8_t* xrow = sX + (c0 >> 6) * OUT_BYTES + r * 128;
-        const int ch0 = (c0 & 63) >> 3;
-#pragma unroll
-        for (int cq = 0; cq < 4; ++cq) {
-          const float4* w4 = reinterpret_cast<const float4*>(vw + c0 + cq * 8);
-          const float4* b4 = reinterpret_cast<const float4*>(vb + c0 + cq * 8);
-          const float4 wa = w4[0], wb = w4[1], ba = b4[0], bb = b4[1];
-          const float wf[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
-          const float bf[8] = {ba.x, ba.y, ba.z, ba.w, bb.x, bb.y, bb.z, bb.w};
-          __half2 o[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e)
-            o[e] = __floats2half2_rn((v[cq * 8 + 2 * e] - mean) * inv * wf[2 * e] + bf[2 * e],
-                                     (v[cq * 8 + 2 * e + 1] - mean) * inv * wf[2 * e + 1] + bf[2 * e + 1]);
-          *reinterpret_cast<uint4*>(xrow + (((ch0 + cq) ^ (r & 7)) * 16)) = *reinterpret_cast<uint4*>(o);
-        }
-      }
-      // the accumulator is read: the MMAs of the next tile may start
       fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(cluster_addr(tempty, 0));
+      {
+        const float s1 = s2.x + s2.y;
+        red1[g * 128 + r] = c + s1 / float(QC);                            // mean of the quarter
+        red2[g * 128 + r] = fmaxf((q2.x + q2.y) - s1 * (s1 / float(QC)), 0.f);  // its squared deviations
+      }
+      named_bar(1, 512);
+      const float m0 = red1[r], m1 = red1[128 + r], m2 = red1[256 + r], m3 = red1[384 + r];
+      const float mean = ((m0 + m1) + (m2 + m3)) * 0.25f;
+      const float2 nm = make_float2(-mean, -mean);
+      const float dm0 = m0 - mean, dm1 = m1 - mean, dm2 = m2 - mean, dm3 = m3 - mean;
+      const float ssd = ((red2[r] + red2[128 + r]) + (red2[256 + r] + red2[384 + r])) +
+                        float(QC) * ((dm0 * dm0 + dm1 * dm1) + (dm2 * dm2 + dm3 * dm3));
+      const float var = ssd / float(NF);
+      const float inv = 1.0f / sqrtf(var + p.eps);
+      const float2 inv2 = make_float2(inv, inv);
+      // pass 3: (v - mean) inv w + b, written over the staged residual
+      uint32_t y0[8], y1[8];
+#pragma unroll
+      for (int kk = 0; kk < NP; ++kk) {
+        const int k = kk < NR ? NT + kk : kk - NR;  // the register pieces first (shorter live ranges)
+        const int c0 = g * QC + k * 16;
+        if ((k & 1) == 0) load_y2(k, y0, y1);
+        float v[16];
+        make_v(k, (k & 1) ? y1 : y0, v);
+        uint8_t* xrow = sX + (c0 >> 6) * OUT_BYTES + r * 128;
+        const int ch0 = (c0 & 63) >> 3;
+#pragma unroll
+        for (int cq = 0; cq < 2; ++cq) {
+          const float4* w4 = reinterpret_cast<const float4*>(vw + c0 + cq * 8);
+          const float4* b4 = reinterpret_cast<const float4*>(vb + c0 + cq * 8);
+          const float4 wa = w4[0], wb = w4[1], ba = b4[0], bb = b4[1];
+          const float2 wf[4] = {make_float2(wa.x, wa.y), make_float2(wa.z, wa.w), make_float2(wb.x, wb.y),
+                                make_float2(wb.z, wb.w)};
+          const float2 bf[4] = {make_float2(ba.x, ba.y), make_float2(ba.z, ba.w), make_float2(bb.x, bb.y),
+                                make_float2(bb.z, bb.w)};
+          __half2 o[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 d = fadd2(make_float2(v[cq * 8 + 2 * e], v[cq * 8 + 2 * e + 1]), nm);
+            const float2 z = ffma2(fmul2(d, inv2), wf[e], bf[e]);
+            o[e] = __floats2half2_rn(z.x, z.y);
+          }
+          *reinterpret_cast<uint4*>(xrow + (((ch0 + cq) ^ (r & 7)) * 16)) = *reinterpret_cast<uint4*>(o);
+        }
+      }
       fence_proxy_async_smem();
       named_bar(1, 512);
       if (leader) {
