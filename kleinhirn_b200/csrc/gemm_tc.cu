@@ -729,6 +729,13 @@ __global__ void __launch_bounds__(LCfg<NF>::THREADS, 1)
 #pragma unroll
         for (int b = 0; b < G::NBOX; ++b) tma_load_2d(sX + b * OUT_BYTES, &tmR, res_full, b * 64, row0);
         res_pending = true;
+        // short K: the residual of this CTA's next tile into L2 now, so that its load into the
+        // staging tile (after this tile's result has left it) is an L2 hit; with long K the
+        // loads of A keep HBM busy and the prefetch only competes with them
+        if (p.K <= 512 && t + npairs < tiles) {
+#pragma unroll
+          for (int b = 0; b < G::NBOX; ++b) tma_prefetch_2d(&tmR, b * 64, row0 + npairs * 2 * BM);
+        }
       }
       bool failed = *abort_flag || !mbar_wait(tfull, uint32_t(local & 1), 54);
       failed = failed || !mbar_wait(res_full, uint32_t(local & 1), 55);
@@ -795,13 +802,12 @@ __global__ void __launch_bounds__(LCfg<NF>::THREADS, 1)
       named_bar(1, 512);
       const float m0 = red1[r], m1 = red1[128 + r], m2 = red1[256 + r], m3 = red1[384 + r];
       const float mean = ((m0 + m1) + (m2 + m3)) * 0.25f;
-      const float2 nm = make_float2(-mean, -mean);
       const float dm0 = m0 - mean, dm1 = m1 - mean, dm2 = m2 - mean, dm3 = m3 - mean;
       const float ssd = ((red2[r] + red2[128 + r]) + (red2[256 + r] + red2[384 + r])) +
                         float(QC) * ((dm0 * dm0 + dm1 * dm1) + (dm2 * dm2 + dm3 * dm3));
       const float var = ssd / float(NF);
       const float inv = 1.0f / sqrtf(var + p.eps);
-      const float2 inv2 = make_float2(inv, inv);
+      const float2 inv2 = make_float2(inv, inv), nmi2 = make_float2(-mean * inv, -mean * inv);
       // pass 3: (v - mean) inv w + b, written over the staged residual
       uint32_t y0[8], y1[8];
 #pragma unroll
@@ -825,8 +831,8 @@ __global__ void __launch_bounds__(LCfg<NF>::THREADS, 1)
           __half2 o[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const float2 d = fadd2(make_float2(v[cq * 8 + 2 * e], v[cq * 8 + 2 * e + 1]), nm);
-            const float2 z = ffma2(fmul2(d, inv2), wf[e], bf[e]);
+            // (v - mean) inv as v inv - mean inv: one rounding instead of two
+            const float2 z = ffma2(ffma2(make_float2(v[cq * 8 + 2 * e], v[cq * 8 + 2 * e + 1]), inv2, nmi2), wf[e], bf[e]);
             o[e] = __floats2half2_rn(z.x, z.y);
           }
           *reinterpret_cast<uint4*>(xrow + (((ch0 + cq) ^ (r & 7)) * 16)) = *reinterpret_cast<uint4*>(o);

@@ -82,6 +82,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int co
   return mbar_wait_for(bar, parity, code, WAIT_LIMIT_NS);
 }
 
+// Prefetch of a 2-D tensor-map box into L2 (no shared memory, no completion).
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(map), "r"(x), "r"(y) : "memory");
+}
+
 // 2-D TMA tile load into shared memory, completion on an mbarrier (no multicast).
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
   asm volatile(
