@@ -69,7 +69,14 @@ struct XParams {
   int M, N, K, act;
   const float* bias;
   float* C;
+  int kps;  // 32-wide K blocks per split (split-K launches: gridDim.z splits, one cluster)
 };
+
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
 
 __global__ void __launch_bounds__(XTHREADS, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
@@ -85,7 +92,11 @@ __global__ void __launch_bounds__(XTHREADS, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * XBN, m0 = blockIdx.y * XBM;
-  const int nk = (p.K + XBK - 1) / XBK;
+  const int nk_all = (p.K + XBK - 1) / XBK;
+  const bool splitk = gridDim.z > 1;
+  // this CTA's K blocks [kb0, kb0 + nk): all of them, or split blockIdx.z of a split-K cluster
+  const int kb0 = splitk ? int(blockIdx.z) * p.kps : 0;
+  const int nk = splitk ? min(p.kps, nk_all - kb0) : nk_all;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < XSTAGES; ++s) {
@@ -120,10 +131,11 @@ __global__ void __launch_bounds__(XTHREADS, 1)
         }
         uint8_t* st = smem + s * XSTAGE;
         mbar_arrive_expect_tx(&full[s], XSTAGE);
-        tma_load_2d(st, &tmAh, &full[s], kb * XBK, m0);
-        tma_load_2d(st + XA, &tmAl, &full[s], kb * XBK, m0);
-        tma_load_2d(st + 2 * XA, &tmWh, &full[s], kb * XBK, n0);
-        tma_load_2d(st + 2 * XA + XB, &tmWl, &full[s], kb * XBK, n0);
+        const int kx = (kb0 + kb) * XBK;
+        tma_load_2d(st, &tmAh, &full[s], kx, m0);
+        tma_load_2d(st + XA, &tmAl, &full[s], kx, m0);
+        tma_load_2d(st + 2 * XA, &tmWh, &full[s], kx, n0);
+        tma_load_2d(st + 2 * XA + XB, &tmWl, &full[s], kx, n0);
         issued |= 1u << s;
         parity = (parity & ~(1u << s)) | ((u & 1) << s);
       }
@@ -170,11 +182,18 @@ __global__ void __launch_bounds__(XTHREADS, 1)
     const bool ok = __all_sync(0xffffffffu, mbar_wait(done, 0, 84)) && !*abort_flag;
     fence_after_sync();
     const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16);
+    float* part = reinterpret_cast<float*>(smem);  // split-K: [128][XBN + 1] over the stages (all read)
 #pragma unroll 1
     for (int c0 = 0; c0 < XBN; c0 += 32) {
       uint32_t v[32];
       tmem_ld32(taddr + uint32_t(c0), v);
       tmem_ld_wait();
+      if (splitk) {
+        float* prow = part + (quarter * 32 + lane) * (XBN + 1) + c0;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) prow[i] = __uint_as_float(v[i]);
+        continue;
+      }
       if (!ok || row >= p.M) continue;
       float* crow = p.C + int64_t(row) * p.N;
 #pragma unroll
@@ -187,6 +206,29 @@ __global__ void __launch_bounds__(XTHREADS, 1)
   }
   fence_before_sync();
   __syncthreads();
+  if (splitk) {
+    // C = sum of the splits' partials, in split order (deterministic), over distributed shared
+    // memory: CTA z of the cluster reduces rows [z R, (z + 1) R) of the tile
+    cluster_sync();
+    const int S = int(gridDim.z), z = int(blockIdx.z);
+    const int R = (XBM + S - 1) / S;
+    const float* part = reinterpret_cast<const float*>(smem);
+    for (int e = threadIdx.x; e < R * XBN; e += XTHREADS) {
+      const int r = z * R + e / XBN, c = e % XBN;
+      if (r >= XBM) break;
+      const uint32_t a = smem_u32(part + r * (XBN + 1) + c);
+      float acc = 0.f;
+      for (int q = 0; q < S; ++q) {
+        uint32_t aq;
+        asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(aq) : "r"(a), "r"(q));
+        acc += ld_cluster_f32(aq);
+      }
+      const int grow = m0 + r, gcol = n0 + c;
+      if (grow < p.M && gcol < p.N && !*abort_flag)
+        p.C[int64_t(grow) * p.N + gcol] = f32act::activate(acc + (p.bias ? p.bias[gcol] : 0.f), p.act);
+    }
+    cluster_sync();  // no CTA leaves while another reads its partial
+  }
   if (warp == 1) {
     fence_after_sync();
     tmem_free(tmem, 64);
@@ -240,8 +282,32 @@ void launch_gemm_tf32x3(const float* a_hi, const float* a_lo, const float* w_hi,
   p.act = act;
   p.bias = bias;
   p.C = C;
-  const dim3 grid(unsigned((N + XBN - 1) / XBN), unsigned((M + XBM - 1) / XBM));
-  gemm_tf32x3_kernel<<<grid, XTHREADS, XSMEM, st>>>(mah, mal, mwh, mwl, p);
+  const int tiles = ((N + XBN - 1) / XBN) * ((M + XBM - 1) / XBM);
+  const int nk = (K + XBK - 1) / XBK;
+  // Split-K for launches of few tiles (short calls): up to 8 splits of at least two K blocks each,
+  // one cluster per tile, so that about every SM takes part
+  int S = 1;
+  if (tiles < 74) S = std::min({8, 148 / tiles, std::max(1, nk / 2)});
+  p.kps = (nk + S - 1) / S;
+  S = (nk + p.kps - 1) / p.kps;  // every split keeps at least one K block
+  const dim3 grid(unsigned((N + XBN - 1) / XBN), unsigned((M + XBM - 1) / XBM), unsigned(S));
+  if (S == 1) {
+    gemm_tf32x3_kernel<<<grid, XTHREADS, XSMEM, st>>>(mah, mal, mwh, mwl, p);
+  } else {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = unsigned(S);
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(XTHREADS, 1, 1);
+    cfg.dynamicSmemBytes = XSMEM;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    KH_CUDA(cudaLaunchKernelEx(&cfg, gemm_tf32x3_kernel, mah, mal, mwh, mwl, p));
+  }
   KH_CUDA(cudaGetLastError());
 }
 

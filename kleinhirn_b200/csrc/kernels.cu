@@ -512,6 +512,133 @@ __global__ void __launch_bounds__(AW * 32) attention_simt_kernel(AttnArgs a, Seq
   if (lane + 32 < D) st(ctx, qrow * hd + int64_t(h) * D + lane + 32, acc1 * invl);
 }
 
+// Attention without relative terms for the plans the tensor-core kernel does not take (f32 plans,
+// head dimensions other than 32 / 64): one CTA per (16 query rows of a sequence, head), the keys
+// of those rows staged in shared memory KC at a time (K rows padded to D + 1 floats, so the lanes
+// of a warp, one key each, read different banks), then per query row (one warp) the scores of
+// its keys, an online softmax over the chunks and the weighted sum of the value rows (one output
+// column per lane). Same semantics as attention_simt_kernel: masked query rows are zero, masked
+// keys and keys outside the window get no weight and their value rows never enter the sum.
+constexpr int SA_ROWS = 16;  // query rows of one CTA
+constexpr int SA_WARPS = 8;
+
+template <typename T, int KC>
+__global__ void __launch_bounds__(SA_WARPS * 32) attention_smem_kernel(AttnArgs a, SeqTable seq) {
+  extern __shared__ float sa_smem[];
+  const int D = a.D, DP = D + 1;
+  float* sK = sa_smem;        // [KC][D + 1]
+  float* sV = sK + KC * DP;   // [KC][D]
+  float* sQ = sV + KC * D;    // [SA_ROWS][D]
+  const int tile = blockIdx.x / (AROWS_TILE / SA_ROWS), sub = blockIdx.x % (AROWS_TILE / SA_ROWS);
+  const int h = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int s = seq.tiles[2 * tile], n = seq.len[s], base = seq.start[s];
+  const int q0 = seq.tiles[2 * tile + 1] + sub * SA_ROWS;
+  if (q0 >= n) return;  // (CTA-uniform)
+  const int q1 = min(q0 + SA_ROWS, n);
+  const int H = a.H, hd = H * D;
+  const T* qkv = static_cast<const T*>(a.qkv);
+  T* ctx = static_cast<T*>(a.ctx);
+  int jlo = 0, jhi = n;  // keys any of the CTA's rows can keep
+  if (a.window) {
+    jlo = max(0, q0 - a.window);
+    jhi = min(n, q1 + a.window);
+  }
+  for (int e = threadIdx.x; e < SA_ROWS * D; e += blockDim.x) {
+    const int r = e / D, d = e - r * D;
+    const int i = q0 + r;
+    sQ[e] = i < q1 ? ld(qkv, int64_t(base + i) * 3 * hd + int64_t(h) * D + d) : 0.f;
+  }
+  constexpr int RPW = SA_ROWS / SA_WARPS;  // rows per warp
+  float m[RPW], l[RPW], acc0[RPW], acc1[RPW];
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) {
+    m[r] = -3.40282346638528859812e38f;
+    l[r] = 0.f;
+    acc0[r] = 0.f;
+    acc1[r] = 0.f;
+  }
+  for (int c0 = jlo; c0 < jhi; c0 += KC) {
+    const int nk = min(KC, jhi - c0);
+    __syncthreads();  // the previous chunk is consumed (and the query rows are staged)
+    for (int e = threadIdx.x; e < KC * D; e += blockDim.x) {
+      const int jj = e / D, d = e - jj * D;
+      float kv = 0.f, vv = 0.f;
+      if (jj < nk) {
+        const int64_t kr = int64_t(base + c0 + jj) * 3 * hd;
+        kv = ld(qkv, kr + int64_t(H + h) * D + d);
+        if (a.mask[base + c0 + jj] > 0.5f) vv = ld(qkv, kr + int64_t(2 * H + h) * D + d);
+      }
+      sK[jj * DP + d] = kv;
+      sV[jj * D + d] = vv;  // masked and absent keys: zero rows
+    }
+    __syncthreads();
+    const int nt = (nk + 31) >> 5;  // 32-key groups with keys in them
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+      const int li = warp + r * SA_WARPS, i = q0 + li;
+      if (i >= q1 || !(a.mask[base + i] > 0.5f)) continue;  // (warp-uniform)
+      float sc[KC / 32];
+#pragma unroll
+      for (int t = 0; t < KC / 32; ++t) sc[t] = 0.f;
+      const float* q = sQ + li * D;
+      for (int d = 0; d < D; ++d) {
+        const float qd = q[d];
+#pragma unroll
+        for (int t = 0; t < KC / 32; ++t) sc[t] += qd * sK[(lane + 32 * t) * DP + d];
+      }
+      float cmax = -INFINITY;
+      bool keep[KC / 32];
+#pragma unroll
+      for (int t = 0; t < KC / 32; ++t) {
+        const int jj = lane + 32 * t, j = c0 + jj;
+        keep[t] = jj < nk && a.mask[base + min(j, n - 1)] > 0.5f && !(a.window && abs(i - j) > a.window);
+        sc[t] = keep[t] ? sc[t] * a.scale : -INFINITY;
+        cmax = fmaxf(cmax, sc[t]);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, o));
+      if (cmax == -INFINITY) continue;  // no kept key in this chunk
+      const float mn = fmaxf(m[r], cmax);
+      const float corr = expf(m[r] - mn);
+      float psum = 0.f;
+#pragma unroll
+      for (int t = 0; t < KC / 32; ++t) {
+        sc[t] = keep[t] ? expf(sc[t] - mn) : 0.f;
+        psum += sc[t];
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
+      l[r] = l[r] * corr + psum;
+      float a0 = acc0[r] * corr, a1 = acc1[r] * corr;
+#pragma unroll
+      for (int t = 0; t < KC / 32; ++t) {
+        if (t >= nt) break;
+        const float* vrow = sV + 32 * t * D;
+#pragma unroll 8
+        for (int jj = 0; jj < 32; ++jj) {
+          const float pj = __shfl_sync(0xffffffffu, sc[t], jj);
+          if (lane < D) a0 += pj * vrow[jj * D + lane];
+          if (lane + 32 < D) a1 += pj * vrow[jj * D + lane + 32];
+        }
+      }
+      acc0[r] = a0;
+      acc1[r] = a1;
+      m[r] = mn;
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) {
+    const int li = warp + r * SA_WARPS, i = q0 + li;
+    if (i >= q1) continue;
+    const int64_t qrow = int64_t(base) + i;
+    const bool live = a.mask[qrow] > 0.5f && l[r] > 0.f;
+    const float invl = live ? 1.0f / l[r] : 0.f;
+    if (lane < D) st(ctx, qrow * hd + int64_t(h) * D + lane, live ? acc0[r] * invl : 0.f);
+    if (lane + 32 < D) st(ctx, qrow * hd + int64_t(h) * D + lane + 32, live ? acc1[r] * invl : 0.f);
+  }
+}
+
 __global__ void f32_to_f16_kernel(const float* src, __half* dst, int64_t n) {
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
     dst[i] = __float2half_rn(src[i]);
@@ -684,6 +811,20 @@ void launch_gemm_simt(bool f16, const void* A, const void* W, const void* bias, 
 void launch_attention_simt(bool f16, const AttnArgs& a, const SeqTable& seq, cudaStream_t st) {
   if (a.D > 64) throw std::runtime_error("attention: head dimension above 64");
   if (seq.ntiles <= 0) return;
+  if (!a.rel) {
+    // keys staged in shared memory: 128 per chunk up to D = 32, else 64 (at most 37 KB)
+    dim3 grid(seq.ntiles * (AROWS_TILE / SA_ROWS), a.H);
+    const int kc = a.D <= 32 ? 128 : 64;
+    const size_t smem = size_t(kc * (a.D + 1) + kc * a.D + SA_ROWS * a.D) * 4;
+    if (kc == 128) {
+      if (f16) attention_smem_kernel<__half, 128><<<grid, SA_WARPS * 32, smem, st>>>(a, seq);
+      else attention_smem_kernel<float, 128><<<grid, SA_WARPS * 32, smem, st>>>(a, seq);
+    } else {
+      if (f16) attention_smem_kernel<__half, 64><<<grid, SA_WARPS * 32, smem, st>>>(a, seq);
+      else attention_smem_kernel<float, 64><<<grid, SA_WARPS * 32, smem, st>>>(a, seq);
+    }
+    return;
+  }
   dim3 grid(seq.ntiles * (AROWS_TILE / AW), a.H);
   if (f16) attention_simt_kernel<__half><<<grid, AW * 32, 0, st>>>(a, seq);
   else attention_simt_kernel<float><<<grid, AW * 32, 0, st>>>(a, seq);
