@@ -2,7 +2,9 @@
 // runtime and turns it into a status code and a thread-local message.
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
+#include <map>
 #include <memory>
 #include <set>
 #include <sstream>
@@ -23,6 +25,16 @@ struct kh_ctx {
   std::set<kh_plan*> plans;  // plans not yet destroyed: kh_destroy frees them
 };
 
+// The launch list of a plan-mode run (kh_run) replayed as one CUDA graph: captured on the second
+// run with a row count (the first runs eagerly and sets every per-device kernel attribute), keyed
+// by the row count and the sequence-table allocation its launches read. Everything else a launch
+// reads on the host (grids, tensor maps, buffer addresses) follows from those two and the plan.
+struct RunGraph {
+  int rows = 0;
+  const void* table = nullptr;
+  cudaGraphExec_t exec = nullptr;
+};
+
 struct kh_plan {
   kh_ctx* owner = nullptr;
   std::set<kh_bulk*> bulks;  // bulk handles not yet destroyed: kh_plan_destroy frees them
@@ -32,6 +44,13 @@ struct kh_plan {
   bool markers_ready = false;   // kh_upload_markers since creation (plans with a markers input)
   void* d_capture = nullptr;    // capture slots (owned by ex once allocated)
   std::vector<int32_t> qtypes;  // Julia type of each sequence of the batch
+  std::vector<RunGraph> graphs;
+  std::map<int, int> eager_runs;  // eager runs per row count (a graph is captured on the second)
+  bool graphs_off = false;        // KH_NO_GRAPHS set, or a capture of this plan failed
+  ~kh_plan() {
+    for (RunGraph& g : graphs)
+      if (g.exec) cudaGraphExecDestroy(g.exec);
+  }
 };
 
 struct kh_bulk {
@@ -280,6 +299,7 @@ int kh_plan_create(kh_ctx* ctx, const char* plan_json, size_t len, kh_plan** out
   Ctx* c = ctx->c.get();
   auto p = std::make_unique<kh_plan>();
   p->owner = ctx;
+  p->graphs_off = std::getenv("KH_NO_GRAPHS") != nullptr;  // every run eager (measurement, debugging)
   const int st = guard(c, Latch::No, [&] {
     kh::Json plan;
     try {
@@ -407,6 +427,52 @@ int kh_upload_markers(kh_plan* plan, const uint32_t* packed, size_t packed_len, 
   });
 }
 
+// The steps and the f32 output staging of a prepared plan-mode run: a replay of the graph of
+// this row count when one exists, else eagerly (and captured for the next run on the second).
+static void run_graphed(kh_plan* plan, int rows, cudaStream_t st) {
+  kh::Exec& ex = plan->ex;
+  auto eager = [&] {
+    kh::exec_steps(ex, st);
+    kh::exec_output(ex, plan->cp.out_rows, ex.d_out, st);
+  };
+  for (const RunGraph& g : plan->graphs)
+    if (g.rows == rows && g.table == ex.d_table) {
+      KH_CUDA(cudaGraphLaunch(g.exec, st));
+      return;
+    }
+  if (plan->graphs_off || ++plan->eager_runs[rows] < 2) {
+    eager();
+    return;
+  }
+  cudaGraph_t graph = nullptr;
+  KH_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed));
+  try {
+    eager();
+  } catch (...) {
+    cudaStreamEndCapture(st, &graph);
+    if (graph) cudaGraphDestroy(graph);
+    cudaGetLastError();
+    plan->graphs_off = true;
+    throw;
+  }
+  KH_CUDA(cudaStreamEndCapture(st, &graph));
+  cudaGraphExec_t exec = nullptr;
+  const cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (e != cudaSuccess) {  // not replayable here: this plan runs eagerly from now on
+    cudaGetLastError();
+    plan->graphs_off = true;
+    eager();
+    return;
+  }
+  if (plan->graphs.size() >= 8) {  // a few row counts at a time (B = 1 callers vary the length)
+    cudaGraphExecDestroy(plan->graphs.front().exec);
+    plan->graphs.erase(plan->graphs.begin());
+  }
+  plan->graphs.push_back({rows, ex.d_table, exec});
+  KH_CUDA(cudaGraphLaunch(exec, st));
+}
+
 int kh_run(kh_plan* plan, int rows) {
   if (!plan) {
     g_err = "kh_run: null plan";
@@ -415,9 +481,7 @@ int kh_run(kh_plan* plan, int rows) {
   Ctx* c = plan->owner->c.get();
   return guard(c, Latch::Yes, [&] {
     plan_prepare(plan, rows);
-    kh::exec_steps(plan->ex, c->stream);
-    const kh::CompiledPlan& cp = plan->cp;
-    kh::exec_output(plan->ex, cp.out_rows, plan->ex.d_out, c->stream);
+    run_graphed(plan, rows, c->stream);
     KH_CUDA(cudaGetLastError());
   });
 }
