@@ -561,7 +561,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
           tmem_st_wait();
         }
         // p = exp2(s scale log2e - m) in f16, into this row of the stream's P block (128-byte swizzled)
-        float ls[4] = {0.f, 0.f, 0.f, 0.f};
+        float2 ls2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           const bool any = any_c[c];
@@ -577,8 +577,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
                 const float x0 = ex2_approx(xx.x);
                 const float x1 = ex2_approx(xx.y);
                 if constexpr (!C::SUMS) {
-                  ls[i & 3] += x0;
-                  ls[(i + 1) & 3] += x1;
+                  ls2[(i >> 1) & 1] = fadd2(ls2[(i >> 1) & 1], make_float2(x0, x1));
                 }
                 __half2 hv = __floats2half2_rn(x0, x1);
                 pk[e2] = *reinterpret_cast<uint32_t*>(&hv);
@@ -588,7 +587,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_tc_kernel(const __grid_consta
             *reinterpret_cast<uint4*>(prow + ((ch ^ (r_local & 7)) * 16)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
           }
         }
-        l = l * corr + ((ls[0] + ls[1]) + (ls[2] + ls[3]));  // (corr rescales the sum so far)
+        l = l * corr + ((ls2[0].x + ls2[0].y) + (ls2[1].x + ls2[1].y));  // (corr rescales the sum so far)
         // value rows of masked or absent keys become zero before the PV product (a tile whose 64
         // key rows are all present and unmasked, the rule in packed bulk runs, needs nothing:
         // the MMA thread itself waits for V)

@@ -14,6 +14,10 @@
 //   warp 1     one thread issues, per 8-wide K step, A_lo W_hi, A_hi W_lo and A_hi W_hi;
 //   warps 2-5  epilogue: each thread one accumulator row (TMEM lane), bias and activation in
 //              f32 (the CUDA-core kernels' arithmetic), stored to C.
+// Launches of few tiles (short calls) split K: the grid's z splits of a tile form one cluster,
+// each CTA accumulates its K blocks and writes the partial tile to its shared memory, and CTA z
+// then sums rows [z R, (z + 1) R) of all partials in split order over distributed shared memory
+// (deterministic), adds bias and activation and stores them.
 // Rows, columns and K past the matrices are zero-filled by the tensor maps and not stored.
 
 #include <algorithm>
