@@ -253,3 +253,16 @@ def test_relative_attention_head_groups():
     err = np.abs(got[keep] - want[keep])
     tol = 4e-3 + 1e-2 * np.abs(want[keep])
     assert np.all(err <= tol), f"worst {err.max()} at {int(np.argmax(err - tol))}"
+
+
+@pytest.mark.parametrize("D", [16, 48])
+@pytest.mark.parametrize("L,lens,window", [
+    (50, [50, 17, 33], 0),
+    (300, [300, 129], 0),          # keys staged in several chunks (128 for D 16, 64 for D 48)
+    (200, [200, 150, 7, 61], 16),
+    (96, [96, 1, 90, 64, 30], 5),
+])
+def test_attention_other_head_dims_f16(D, L, lens, window):
+    """Head dimensions the tensor-core kernel does not take run the shared-memory kernel
+    (attention_smem_kernel): the same semantics, NaN padding rows never enter a sum."""
+    test_packed_attention_f16(D, L, lens, window)

@@ -164,3 +164,50 @@ def test_chunks_are_even_and_bounded(world):
         assert count == n, (rows, chunk, count, n)
     assert dp.chunk_size(3960, 0) >= 3960
     assert dp.chunk_size(10, 777) == 777
+
+
+FWD_CFG = {"model_type": "bert", "hidden_size": 64, "num_hidden_layers": 2, "num_attention_heads": 2,
+           "intermediate_size": 128, "hidden_act": "gelu", "vocab_size": 120, "max_position_embeddings": 66,
+           "type_vocab_size": 2, "layer_norm_eps": 1e-12, "num_labels": 3}
+
+
+def _fwd_inputs():
+    rng = np.random.default_rng(21)
+    lens = rng.integers(3, 60, 11)
+    return [list(rng.integers(3, 120, int(n))) for n in lens]
+
+
+def _forward_rank_main(rank: int, world: int, port: int, out_dir: str):
+    import datetime
+
+    import torch.distributed as dist
+    from harness import Model, oracle_forward
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        m = Model(FWD_CFG, {"task": "sequence-classification"}, seed=4, f16=False)
+        ids = _fwd_inputs()
+        lens = np.array([len(x) for x in ids])
+        shards = [dp.shard_sequences(lens, world, r) for r in range(world)]
+        mine = shards[rank]
+        out_mine = oracle_forward(m, [ids[i] for i in mine], 64, threads=1)
+        g = dp.OutputGather(dist, None, rank, shards, m.cols)
+        g.local.numpy()[: len(mine) * m.cols] = np.asarray(out_mine, dtype=np.float32).ravel()
+        out = g.gather()
+        np.save(os.path.join(out_dir, f"fwd{rank}.npy"), out if out is not None else np.zeros(0))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_forward_equals_one_process(tmp_path):
+    """The sharded forward (each rank runs its own sequences, rank 0 gathers them in input
+    order) gives the same outputs as one process running every sequence: the path has no
+    collective, so each sequence's result does not depend on the rank that ran it."""
+    from harness import Model, oracle_forward
+    world = 2
+    mp.start_processes(_forward_rank_main, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       start_method="spawn", join=True)
+    m = Model(FWD_CFG, {"task": "sequence-classification"}, seed=4, f16=False)
+    want = np.asarray(oracle_forward(m, _fwd_inputs(), 64, threads=1), dtype=np.float32)
+    got = np.load(tmp_path / "fwd0.npy").reshape(want.shape)
+    assert np.array_equal(got, want)
