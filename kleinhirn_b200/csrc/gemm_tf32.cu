@@ -9,11 +9,13 @@
 // for (the reference's WASM executor computes them in f32).
 //
 // Tiles are 128 x 64 (one M = 128 MMA per CTA, the accumulator in 64 TMEM columns), one per CTA:
-//   warp 0     TMA: 32-column (128-byte) K slices of A_hi, A_lo, W_hi and W_lo per stage into a
+//   warp 0     TMA: 32-column (128-byte) K slices of A (f32), W_hi and W_lo per stage into a
 //              four-stage ring (128-byte swizzle);
-//   warp 1     one thread issues, per 8-wide K step, A_lo W_hi, A_hi W_lo and A_hi W_hi;
-//   warps 2-5  epilogue: each thread one accumulator row (TMEM lane), bias and activation in
-//              f32 (the CUDA-core kernels' arithmetic), stored to C.
+//   warps 2-5  first split each stage's A into A_hi (in place) and A_lo (the stage's second A
+//              slot), then, once the accumulator is done, the epilogue: each thread one
+//              accumulator row (TMEM lane), bias and activation in f32 (the CUDA-core kernels'
+//              arithmetic), stored to C;
+//   warp 1     one thread issues, per 8-wide K step, A_lo W_hi, A_hi W_lo and A_hi W_hi.
 // Launches of few tiles (short calls) split K: the grid's z splits of a tile form one cluster,
 // each CTA accumulates its K blocks and writes the partial tile to its shared memory, and CTA z
 // then sums rows [z R, (z + 1) R) of all partials in split order over distributed shared memory
@@ -83,7 +85,7 @@ __device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
 }
 
 __global__ void __launch_bounds__(XTHREADS, 1)
-    gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
+    gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmA,
                        const __grid_constant__ CUtensorMap tmWh, const __grid_constant__ CUtensorMap tmWl,
                        const XParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -92,7 +94,8 @@ __global__ void __launch_bounds__(XTHREADS, 1)
   uint64_t* empty = full + XSTAGES;
   uint64_t* done = empty + XSTAGES;
   uint64_t* drain = done + 1;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* conv = drain + 1;  // [XSTAGES]: the stage's A split into hi and lo by the epilogue warps
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(conv + XSTAGES);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * XBN, m0 = blockIdx.y * XBM;
@@ -106,13 +109,13 @@ __global__ void __launch_bounds__(XTHREADS, 1)
     for (int s = 0; s < XSTAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+      mbar_init(&conv[s], 128);
     }
     mbar_init(done, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
-    prefetch_tmap(&tmAh);
-    prefetch_tmap(&tmAl);
+    prefetch_tmap(&tmA);
     prefetch_tmap(&tmWh);
     prefetch_tmap(&tmWl);
   }
@@ -134,10 +137,9 @@ __global__ void __launch_bounds__(XTHREADS, 1)
           break;
         }
         uint8_t* st = smem + s * XSTAGE;
-        mbar_arrive_expect_tx(&full[s], XSTAGE);
+        mbar_arrive_expect_tx(&full[s], XA + 2 * XB);  // A (f32), W_hi, W_lo
         const int kx = (kb0 + kb) * XBK;
-        tma_load_2d(st, &tmAh, &full[s], kx, m0);
-        tma_load_2d(st + XA, &tmAl, &full[s], kx, m0);
+        tma_load_2d(st, &tmA, &full[s], kx, m0);
         tma_load_2d(st + 2 * XA, &tmWh, &full[s], kx, n0);
         tma_load_2d(st + 2 * XA + XB, &tmWl, &full[s], kx, n0);
         issued |= 1u << s;
@@ -156,7 +158,7 @@ __global__ void __launch_bounds__(XTHREADS, 1)
       for (int kb = 0; kb < nk; ++kb) {
         const int s = kb % XSTAGES;
         const uint32_t u = uint32_t(kb / XSTAGES);
-        if (*abort_flag || !mbar_wait(&full[s], u & 1, 82)) {
+        if (*abort_flag || !mbar_wait(&conv[s], u & 1, 82)) {
           ok = false;
           break;
         }
@@ -183,6 +185,32 @@ __global__ void __launch_bounds__(XTHREADS, 1)
   } else {
     const int quarter = warp & 3;  // TMEM lanes 32 quarter .. : the rows this warp reads
     const int row = m0 + quarter * 32 + lane;
+    // Until the accumulator is done these warps split each stage's A tile for the MMAs: hi (the
+    // TF32 value of the leading bits) in place, lo = x - hi into the stage's second A slot, at the
+    // same (swizzled) positions, so both tiles keep the tensor map's layout.
+    const int ct = threadIdx.x - 64;  // 0 .. 127
+    bool cok = true;
+    for (int kb = 0; kb < nk && cok; ++kb) {
+      const int s = kb % XSTAGES;
+      const uint32_t u = uint32_t(kb / XSTAGES);
+      cok = __all_sync(0xffffffffu, !*abort_flag && mbar_wait(&full[s], u & 1, 86));
+      if (!cok) break;
+      float4* a = reinterpret_cast<float4*>(smem + s * XSTAGE);
+      float4* alo = reinterpret_cast<float4*>(smem + s * XSTAGE + XA);
+#pragma unroll
+      for (int i = 0; i < XA / 16 / 128; ++i) {
+        const float4 v = a[ct + 128 * i];
+        const float4 h = make_float4(__uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u),
+                                     __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u),
+                                     __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u),
+                                     __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u));
+        a[ct + 128 * i] = h;
+        alo[ct + 128 * i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+      }
+      fence_proxy_async_smem();  // the tensor core (async proxy) reads what these threads wrote
+      mbar_arrive(&conv[s]);
+    }
+    if (!cok) *abort_flag = 1;
     const bool ok = __all_sync(0xffffffffu, mbar_wait(done, 0, 84)) && !*abort_flag;
     fence_after_sync();
     const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16);
@@ -267,16 +295,15 @@ const DevTensor& gemm_tf32_weight(Ctx* ctx, const std::string& name) {
   });
 }
 
-void launch_gemm_tf32x3(const float* a_hi, const float* a_lo, const float* w_hi, const float* w_lo, const float* bias,
-                        float* C, int M, int N, int K, int act, cudaStream_t st) {
+void launch_gemm_tf32x3(const float* a, const float* w_hi, const float* w_lo, const float* bias, float* C, int M,
+                        int N, int K, int act, cudaStream_t st) {
   if (M <= 0 || N <= 0) return;
   if (!gemm_tf32_supported(N, K)) throw PlanError("gemm (3xTF32): N < 16 or K not a multiple of 4");
   static std::atomic<uint64_t> configured{0};
   once_per_device(configured, [] {
     KH_CUDA(cudaFuncSetAttribute(gemm_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, XSMEM));
   });
-  const CUtensorMap mah = tensor_map_f32(a_hi, uint64_t(M), uint64_t(K), uint64_t(K), XBK, XBM);
-  const CUtensorMap mal = tensor_map_f32(a_lo, uint64_t(M), uint64_t(K), uint64_t(K), XBK, XBM);
+  const CUtensorMap ma = tensor_map_f32(a, uint64_t(M), uint64_t(K), uint64_t(K), XBK, XBM);
   const CUtensorMap mwh = tensor_map_f32(w_hi, uint64_t(N), uint64_t(K), uint64_t(K), XBK, XBN);
   const CUtensorMap mwl = tensor_map_f32(w_lo, uint64_t(N), uint64_t(K), uint64_t(K), XBK, XBN);
   XParams p;
@@ -296,7 +323,7 @@ void launch_gemm_tf32x3(const float* a_hi, const float* a_lo, const float* w_hi,
   S = (nk + p.kps - 1) / p.kps;  // every split keeps at least one K block
   const dim3 grid(unsigned((N + XBN - 1) / XBN), unsigned((M + XBM - 1) / XBM), unsigned(S));
   if (S == 1) {
-    gemm_tf32x3_kernel<<<grid, XTHREADS, XSMEM, st>>>(mah, mal, mwh, mwl, p);
+    gemm_tf32x3_kernel<<<grid, XTHREADS, XSMEM, st>>>(ma, mwh, mwl, p);
   } else {
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
@@ -310,7 +337,7 @@ void launch_gemm_tf32x3(const float* a_hi, const float* a_lo, const float* w_hi,
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    KH_CUDA(cudaLaunchKernelEx(&cfg, gemm_tf32x3_kernel, mah, mal, mwh, mwl, p));
+    KH_CUDA(cudaLaunchKernelEx(&cfg, gemm_tf32x3_kernel, ma, mwh, mwl, p));
   }
   KH_CUDA(cudaGetLastError());
 }

@@ -16,17 +16,17 @@ bool gemm_tf32_supported(int N, int K);
 
 // The split x = hi + lo of an f32 tensor for the tensor cores: hi keeps the sign, the exponent and
 // the 10 leading mantissa bits (exactly a TF32 value), lo = x - hi (exact in f32). Derived once
-// per weight; one launch per activation split.
+// per weight (the activations are split inside the GEMM).
 void launch_tf32_split(const float* x, float* hi, float* lo, int64_t n, cudaStream_t st);
 // The split of weight `name` [N, K] (f32): hi in the first N K floats of ptr, lo in the next.
 const DevTensor& gemm_tf32_weight(Ctx* ctx, const std::string& name);
 
 // C = act(A W^T + bias), f32: A = A_hi + A_lo, W = W_hi + W_lo, and the product as
 // A_hi W_hi + A_hi W_lo + A_lo W_hi with f32 accumulation in TMEM (the A_lo W_lo term is below
-// f32 precision). A_hi / A_lo are the caller's split of A ([M, K] each), W_hi / W_lo the
-// weight's. act: 0 none, 1 relu, 2 GELU, 3 tanh, 4 silu, as the CUDA-core kernels.
-void launch_gemm_tf32x3(const float* a_hi, const float* a_lo, const float* w_hi, const float* w_lo, const float* bias,
-                        float* C, int M, int N, int K, int act, cudaStream_t st);
+// f32 precision). A [M, K] is split inside the kernel, stage by stage; W_hi / W_lo are the
+// weight's split. act: 0 none, 1 relu, 2 GELU, 3 tanh, 4 silu, as the CUDA-core kernels.
+void launch_gemm_tf32x3(const float* a, const float* w_hi, const float* w_lo, const float* bias, float* C, int M,
+                        int N, int K, int act, cudaStream_t st);
 
 // Code of the first pipeline wait of this GEMM that gave up on the current device (0: none), read
 // after a sync and cleared.

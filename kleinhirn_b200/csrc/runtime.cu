@@ -471,29 +471,20 @@ void plan_compile(Ctx* ctx, const Json& plan, CompiledPlan& cp) {
         }
       }
       if (!f16 && gemm_tf32_supported(N, K)) {
-        // f32 plans on the tensor cores: A split into TF32 hi + lo parts (scratch rows of this
-        // runtime), the weight's split derived once, three TF32 products per K step
+        // f32 plans on the tensor cores: the weight's TF32 split derived once, the activations
+        // split stage by stage inside the GEMM, three TF32 products per K step
         const float* wsplit = static_cast<const float*>(gemm_tf32_weight(ctx, wname).ptr);
         const int64_t wn = int64_t(N) * K;
-        for (const char* id : {"#tf32hi", "#tf32lo"}) {
-          BufInfo& sb = touch(id);
-          sb.kind = BufInfo::Rows;
-          sb.elem = 4;
-          sb.cols = std::max<int64_t>(sb.cols, K);
-        }
         written(op);
         protos.push_back({"gemm", names, [=](const CompiledPlan& c) {
-          const int ia = bi(c, a_id), io = bi(c, out_id), ih = bi(c, "#tf32hi"), il = bi(c, "#tf32lo");
+          const int ia = bi(c, a_id), io = bi(c, out_id);
           auto fb = resolve(c, bias);
           const bool bias_zero = !bias.weight;
           Step s;
-          s.launches = 2;
           s.run = [=](Exec& ex, cudaStream_t st) {
             const int M = fixed_rows ? (ex.bulk ? ex.seq.count : fixed_m) : ex.T;
-            float* hi = static_cast<float*>(ex.buf(ih));
-            float* lo = static_cast<float*>(ex.buf(il));
-            launch_tf32_split(static_cast<const float*>(ex.buf(ia)), hi, lo, int64_t(M) * K, st);
-            launch_gemm_tf32x3(hi, lo, wsplit, wsplit + wn, bias_zero ? nullptr : static_cast<const float*>(fb(ex)),
+            launch_gemm_tf32x3(static_cast<const float*>(ex.buf(ia)), wsplit, wsplit + wn,
+                               bias_zero ? nullptr : static_cast<const float*>(fb(ex)),
                                static_cast<float*>(ex.buf(io)), M, N, K, act, st);
           };
           return s;
