@@ -103,7 +103,10 @@ int kh_upload_markers(kh_plan* plan, const uint32_t* packed, size_t packed_len, 
                       size_t n_qtypes);
 
 /* PlanRunner.run (src/backend.ts:21-23): one forward over `rows` rows — the real rows of a
- * B = 1 call (1 <= rows <= length), or length * batch for a batch plan. */
+ * B = 1 call (1 <= rows <= length), or length * batch for a batch plan. Queues the work and
+ * returns. From the second call with a given `rows` on, the launch list runs as one CUDA graph
+ * captured on that call (up to 8 row counts per plan); KH_NO_GRAPHS in the environment when the
+ * plan is created keeps every run eager. */
 int kh_run(kh_plan* plan, int rows);
 
 /* PlanRunner.readOutput (src/backend.ts:24, src/plan/executor.ts:398-408): blocks until the
