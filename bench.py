@@ -44,9 +44,10 @@ BUCKET = 512
 
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one GEMM launch on a 262,144-row
 # chunk, mean of the four GEMM launches of a C5 layer (qkv 0.753 GB, FFN-in 0.951 GB, attnOut +
-# LayerNorm 0.568 GB, FFN-out + LayerNorm 1.195 GB), from one ncu capture each; every term is
-# rows x a per-row byte count, so a launch over another chunk size scales with its rows.
-GEMM_TRAFFIC_BYTES = 866.2e6
+# LayerNorm 0.571 GB, FFN-out + LayerNorm 1.200 GB), from one ncu capture each (the LayerNorm
+# launches captured on a 288,315-row chunk and scaled); every term is rows x a per-row byte
+# count, so a launch over another chunk size scales with its rows.
+GEMM_TRAFFIC_BYTES = 868.8e6
 GEMM_TRAFFIC_ROWS = 262144
 GEMM_TRAFFIC_SOURCE = "ncu, profiles/gemm_pair_c5.md and profiles/gemm_addln_c5.md"
 
