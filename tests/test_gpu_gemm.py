@@ -57,7 +57,8 @@ def assert_f16_close(got, want, what):
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 32, 64), (7, 384, 384), (128, 128, 64), (129, 1152, 384),
-                                   (300, 768, 3072), (1000, 1536, 384), (77, 96, 40), (640, 2304, 768)])
+                                   (300, 768, 3072), (1000, 1536, 384), (77, 96, 40), (640, 2304, 768),
+                                   (300, 1088, 256)])  # 256-wide tiles past N: one live warpgroup
 @pytest.mark.parametrize("act", [0, 2, 3])
 def test_gemm_shapes(M, N, K, act):
     rng = np.random.default_rng(M * 7 + N + K + act)
@@ -77,7 +78,7 @@ def test_gemm_relu_silu(act):
     test_gemm_shapes(256, 384, 384, act)
 
 
-@pytest.mark.parametrize("N", [384, 768])  # 128- and 256-wide tiles
+@pytest.mark.parametrize("N", [384, 768, 1152])  # 192-, 256-wide tiles, 256 past N
 def test_residual_epilogue(N):
     """matmul (attnOut) followed by add (addA): x = f16(x + f16(A W^T + b))."""
     M, K, L = 300, 384, 300
