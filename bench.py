@@ -85,7 +85,7 @@ def parse_args():
     ap.add_argument("--pairs", type=int, default=0,
                     help="sequences of a throughput workload (0: 65,536 for c5, 4,096 / 2,048 at L512)")
     ap.add_argument("--chunk-tokens", type=int, default=0,
-                    help="packed rows per bulk chunk (0: even chunks of at most 524,288 rows)")
+                    help="packed rows per bulk chunk (0: even chunks of at most 1,048,576 rows)")
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -41,7 +41,7 @@ def shard_sequences(lens: np.ndarray, world: int, rank: int) -> np.ndarray:
     return mine[np.argsort(lens[mine], kind="stable")]
 
 
-def chunk_size(tokens: int, requested: int = 0, bucket: int = 512, max_rows: int = 524288) -> int:
+def chunk_size(tokens: int, requested: int = 0, bucket: int = 512, max_rows: int = 1048576) -> int:
     """Packed rows per bulk chunk: as requested, or the rank's rows in even chunks of at most
     `max_rows` (long launches keep the tail waves of the GEMMs small; even chunks avoid a short
     last one), plus one bucket of room for the sequence that does not fit exactly."""

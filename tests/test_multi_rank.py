@@ -145,7 +145,7 @@ def test_shard_single_rank_identity():
 
 @pytest.mark.parametrize("world", [1, 2, 4, 8])
 def test_chunks_are_even_and_bounded(world):
-    """Each rank's rows go in even bulk chunks of at most 524,288 (+ one bucket of room for the
+    """Each rank's rows go in even bulk chunks of at most 1,048,576 (+ one bucket of room for the
     sequence that does not fit exactly): the full C5 step on 1 GPU, and its shares on 2, 4, 8."""
     from kleinhirn_b200 import synthetic
     lens = synthetic.seq_lengths("mminilm-l12-xlmr", 65536, 1234)
@@ -154,7 +154,7 @@ def test_chunks_are_even_and_bounded(world):
         rows = int(lens[mine].sum())
         chunk = dp.chunk_size(rows, 0)
         n = -(-rows // chunk)
-        assert chunk <= 524288 + 512
+        assert chunk <= 1048576 + 512
         # greedy packing of whole sequences fills the chunks: no short extra one
         filled, count = 0, 1
         for ln in lens[mine]:
