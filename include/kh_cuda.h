@@ -181,7 +181,10 @@ int kh_bulk_set_word_table(kh_bulk* bulk, const char* name);
  * outside [0, vocab) gives a zero row, and the next kh_bulk_read returns KH_ERR_ARG. */
 int kh_bulk_upload_ids(kh_bulk* bulk, const int32_t* ids, size_t n, const uint32_t* type_ids, size_t type_len);
 
-/* Device-side forward of every sequence (no host copies; returns when the launches are queued). */
+/* Device-side forward of every sequence (no host copies; returns when the launches are queued).
+ * A run whose chunks have exactly the previous run's launch parameters (the same lengths
+ * uploaded again) is captured as a CUDA graph on its second occurrence and replayed after;
+ * KH_NO_GRAPHS in the environment when the handle is created keeps every run eager. */
 int kh_bulk_run(kh_bulk* bulk);
 
 /* Waits for the run and writes the outputs: one row of out_cols f32 per sequence for pooled

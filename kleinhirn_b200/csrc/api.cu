@@ -79,6 +79,12 @@ struct kh_bulk {
   int64_t vocab = 0;
   int32_t* d_ids = nullptr;       // packed token ids of kh_bulk_upload_ids
   bool ids_used = false;          // the last upload gathered rows on the device
+  // kh_bulk_run replayed as one CUDA graph when its chunks have the shapes of the previous run
+  // (the same lengths uploaded again): captured on the second such run, keyed by every launch
+  // parameter the chunks give (offsets, rows, sequences, tile counts, table address)
+  std::vector<int64_t> graph_key, eager_key;
+  cudaGraphExec_t graph = nullptr;
+  bool graphs_off = false;
   ~kh_bulk();
 };
 
@@ -173,6 +179,7 @@ kh_bulk::~kh_bulk() {
   cudaFree(d_out);
   cudaFree(d_table);
   cudaFree(d_ids);
+  if (graph) cudaGraphExecDestroy(graph);
   if (ev0) cudaEventDestroy(ev0);
   if (ev1) cudaEventDestroy(ev1);
 }
@@ -670,6 +677,7 @@ int kh_bulk_create(kh_plan* plan, int64_t max_tokens, int max_seqs, int64_t chun
   Ctx* c = plan->owner->c.get();
   auto b = std::make_unique<kh_bulk>();
   b->plan = plan;
+  b->graphs_off = std::getenv("KH_NO_GRAPHS") != nullptr;
   const int st = guard(c, Latch::No, [&] {
     const kh::CompiledPlan& cp = plan->cp;
     if (max_tokens < 1 || max_seqs < 1) throw kh::ArgError("kh_bulk_create: max_tokens and max_seqs must be >= 1");
@@ -856,22 +864,65 @@ int kh_bulk_run(kh_bulk* bulk) {
     const size_t esz = cp.f16 ? 2 : 4;
     const int ie = cp.buf_index.at(cp.in_emb), im = cp.buf_index.at(cp.in_mask);
     const int it = cp.in_type.empty() ? -1 : cp.buf_index.at(cp.in_type);
-    int64_t launches = 0;
     int64_t per_chunk = 1;
     for (const kh::Step& s : cp.steps) per_chunk += s.launches;
-    KH_CUDA(cudaEventRecord(bulk->ev0, c->stream));
+    const int64_t launches = per_chunk * int64_t(bulk->chunks.size());
+    auto run_chunks = [&] {
+      for (const kh_bulk::Chunk& ch : bulk->chunks) {
+        ex.ptr[ie] = (char*)bulk->d_emb + size_t(ch.tok0) * cp.emb_size * esz;
+        ex.ptr[im] = bulk->d_mask + ch.tok0;
+        if (it >= 0) ex.ptr[it] = bulk->d_type + ch.tok0;
+        const int32_t* base = bulk->d_table + ch.word0;
+        ex.seq = rebase(ch.seq, base);
+        ex.row_seq = const_cast<int32_t*>(base) + (intptr_t)ch.seq.row_pos + ch.T;
+        ex.T = int(ch.T);
+        kh::exec_steps(ex, c->stream);
+        float* dst = bulk->d_out + (cp.out_per_seq ? int64_t(ch.seq0) : ch.tok0) * cp.out_cols;
+        kh::exec_output(ex, cp.out_per_seq ? ch.S : int(ch.T), dst, c->stream);
+      }
+    };
+    std::vector<int64_t> key{int64_t(reinterpret_cast<intptr_t>(bulk->d_table)), int64_t(bulk->chunks.size())};
     for (const kh_bulk::Chunk& ch : bulk->chunks) {
-      ex.ptr[ie] = (char*)bulk->d_emb + size_t(ch.tok0) * cp.emb_size * esz;
-      ex.ptr[im] = bulk->d_mask + ch.tok0;
-      if (it >= 0) ex.ptr[it] = bulk->d_type + ch.tok0;
-      const int32_t* base = bulk->d_table + ch.word0;
-      ex.seq = rebase(ch.seq, base);
-      ex.row_seq = const_cast<int32_t*>(base) + (intptr_t)ch.seq.row_pos + ch.T;
-      ex.T = int(ch.T);
-      kh::exec_steps(ex, c->stream);
-      float* dst = bulk->d_out + (cp.out_per_seq ? int64_t(ch.seq0) : ch.tok0) * cp.out_cols;
-      kh::exec_output(ex, cp.out_per_seq ? ch.S : int(ch.T), dst, c->stream);
-      launches += per_chunk;
+      const kh::SeqTable& q = ch.seq;
+      for (int64_t v : {ch.tok0, ch.T, int64_t(ch.seq0), int64_t(ch.S), ch.word0, int64_t(q.count),
+                        int64_t(q.max_len), int64_t(q.ntiles), int64_t(q.nptiles),
+                        int64_t(reinterpret_cast<intptr_t>(q.start)), int64_t(reinterpret_cast<intptr_t>(q.len)),
+                        int64_t(reinterpret_cast<intptr_t>(q.row_pos)), int64_t(reinterpret_cast<intptr_t>(q.tiles)),
+                        int64_t(reinterpret_cast<intptr_t>(q.ptiles))})
+        key.push_back(v);
+    }
+    KH_CUDA(cudaEventRecord(bulk->ev0, c->stream));
+    if (bulk->graph && key == bulk->graph_key) {
+      KH_CUDA(cudaGraphLaunch(bulk->graph, c->stream));
+    } else if (!bulk->graphs_off && key == bulk->eager_key) {
+      cudaGraph_t g = nullptr;
+      KH_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeRelaxed));
+      try {
+        run_chunks();
+      } catch (...) {
+        cudaStreamEndCapture(c->stream, &g);
+        if (g) cudaGraphDestroy(g);
+        cudaGetLastError();
+        bulk->graphs_off = true;
+        throw;
+      }
+      KH_CUDA(cudaStreamEndCapture(c->stream, &g));
+      cudaGraphExec_t e = nullptr;
+      const cudaError_t r = cudaGraphInstantiate(&e, g, 0);
+      cudaGraphDestroy(g);
+      if (r != cudaSuccess) {  // not replayable here: eager from now on
+        cudaGetLastError();
+        bulk->graphs_off = true;
+        run_chunks();
+      } else {
+        if (bulk->graph) cudaGraphExecDestroy(bulk->graph);
+        bulk->graph = e;
+        bulk->graph_key = key;
+        KH_CUDA(cudaGraphLaunch(e, c->stream));
+      }
+    } else {
+      run_chunks();
+      bulk->eager_key = std::move(key);
     }
     KH_CUDA(cudaEventRecord(bulk->ev1, c->stream));
     KH_CUDA(cudaGetLastError());
